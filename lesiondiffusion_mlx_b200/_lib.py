@@ -1,0 +1,104 @@
+"""ctypes binding of ``libldb200.so``, the C ABI declared in ``include/ldb200.h``.
+
+The library is the only compute path: there is no Python or PyTorch fallback.
+Loading fails loudly when the shared object has not been built, and every
+call that returns a negative status raises ``LdbError`` carrying the
+library's own message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libldb200.so"
+
+LDB_OK = 0
+LDB_F16, LDB_F32, LDB_BF16 = 0, 1, 2
+LDB_CONV_3X3X3, LDB_CONV_3X3X3_S2, LDB_CONV_UP2, LDB_CONV_1X1 = 0, 1, 2, 3
+LDB_ACT_NONE, LDB_ACT_GELU = 0, 1
+
+
+class LdbError(RuntimeError):
+    """A C-ABI call returned a negative status."""
+
+    def __init__(self, name: str, code: int, message: str):
+        super().__init__(f"{name} failed ({code}): {message}")
+        self.code = code
+
+
+class ConvDesc(ctypes.Structure):
+    """Mirror of ``ldb_conv_desc``."""
+
+    _fields_ = [
+        ("batch", ctypes.c_int),
+        ("depth", ctypes.c_int),
+        ("height", ctypes.c_int),
+        ("width", ctypes.c_int),
+        ("in_channels", ctypes.c_int),
+        ("x_ld", ctypes.c_int),
+        ("out_channels", ctypes.c_int),
+        ("out_ld", ctypes.c_int),
+        ("res_ld", ctypes.c_int),
+        ("mode", ctypes.c_int),
+        ("exact", ctypes.c_int),
+        ("out_dtype", ctypes.c_int),
+        ("act", ctypes.c_int),
+        ("output_scale", ctypes.c_float),
+    ]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_SZ = ctypes.c_size_t
+
+# name -> (argtypes); every function returns int unless listed in _RESTYPES.
+SIGNATURES: dict[str, list] = {
+    "ldb_version": [],
+    "ldb_last_error": [],
+    "ldb_device_status": [ctypes.POINTER(ctypes.c_uint), _I],
+    "ldb_conv3d_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_SZ)],
+    "ldb_conv3d_weight_rows": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_I), ctypes.POINTER(_I)],
+    "ldb_conv3d_fwd": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _SZ],
+}
+_RESTYPES = {"ldb_last_error": ctypes.c_char_p}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library() -> ctypes.CDLL:
+    """Load (once) and return the C library with typed signatures."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY_PATH.exists():
+                raise ImportError(
+                    f"{LIBRARY_PATH} is missing: build it with "
+                    "`python -m lesiondiffusion_mlx_b200.build` (there is no fallback path)"
+                )
+            lib = ctypes.CDLL(str(LIBRARY_PATH))
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
+            _lib = lib
+        return _lib
+
+
+def call(name: str, *args) -> int:
+    """Invoke ``name`` and raise ``LdbError`` on a negative status."""
+    lib = library()
+    rc = getattr(lib, name)(*args)
+    if rc < 0:
+        raise LdbError(name, rc, lib.ldb_last_error().decode(errors="replace"))
+    return rc
+
+
+def device_status(reset: bool = True) -> int:
+    """Read (and by default clear) the current device's status word."""
+    value = ctypes.c_uint(0)
+    call("ldb_device_status", ctypes.byref(value), int(reset))
+    return int(value.value)

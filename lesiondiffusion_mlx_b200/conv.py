@@ -1,0 +1,222 @@
+"""Convolution operators over the C ABI: weight packing and the NDHWC conv.
+
+This is the B200 counterpart of ``lesiondiffusion_mlx/_nax_conv.py``: the
+reference packs Torch-layout ``(O, C, 3, 3, 3)`` weights once and runs an
+implicit-GEMM convolution with bias / per-batch shift / residual / output
+scale fused before a single rounding.  Here activations stay NDHWC on the
+device, weights are packed K-major per output channel
+(``[parity][O'][tap][C']``) for the tcgen05 kernel, and every call goes
+through ``ldb_conv3d_fwd``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+MODE_CONV, MODE_STRIDE2, MODE_UP2, MODE_POINTWISE = (
+    _lib.LDB_CONV_3X3X3,
+    _lib.LDB_CONV_3X3X3_S2,
+    _lib.LDB_CONV_UP2,
+    _lib.LDB_CONV_1X1,
+)
+
+
+@dataclass
+class PackedWeight:
+    """A weight packed for ``ldb_conv3d_fwd``.
+
+    ``tensor`` is f16 ``(parities * rows, k_total)``; ``kind`` is ``"conv"``
+    (27 taps, stride 1 or 2), ``"up"`` (8 parities x 8 folded taps) or
+    ``"pointwise"`` (one tap).  ``exact`` weights hold the f16 hi plane then
+    the 2^11-scaled lo plane of an FP32 weight along K.
+    """
+
+    tensor: torch.Tensor
+    kind: str
+    in_channels: int
+    out_channels: int
+    exact: bool
+
+    @property
+    def ndim(self) -> int:
+        """2 for plain packing, 3 for folded upsampling (the reference's shapes)."""
+        return 3 if self.kind == "up" else 2
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return torch.float32 if self.exact else torch.float16
+
+
+def _geometry(in_channels: int, out_channels: int, mode: int, exact: bool) -> tuple[int, int]:
+    desc = _lib.ConvDesc(
+        batch=1, depth=1, height=1, width=1, in_channels=in_channels,
+        x_ld=max(8, ((2 * ((in_channels + 15) // 16) * 16) if exact else in_channels + 7) // 8 * 8),
+        out_channels=out_channels, out_ld=out_channels, res_ld=out_channels, mode=mode,
+        exact=int(exact), out_dtype=_lib.LDB_F16, act=0, output_scale=1.0,
+    )
+    rows = ctypes.c_int(0)
+    k_total = ctypes.c_int(0)
+    _lib.call("ldb_conv3d_weight_rows", ctypes.byref(desc), ctypes.byref(rows), ctypes.byref(k_total))
+    return rows.value, k_total.value
+
+
+def _split_planes(taps: torch.Tensor) -> torch.Tensor:
+    """FP32 ``(..., K)`` as f16 ``(..., 2K)``: hi then 2^11-scaled lo (_nax_conv.py:343-347)."""
+    hi = taps.to(torch.float16)
+    lo = ((taps - hi.to(torch.float32)) * 2048.0).to(torch.float16)
+    return torch.cat([hi, lo], dim=-1)
+
+
+def _pack_rows(taps: torch.Tensor, rows: int, exact: bool) -> torch.Tensor:
+    """``taps`` is f32 ``(P, O, T, C')``; pad O to ``rows`` and flatten K."""
+    parities, out_channels, ntaps, cpad = taps.shape
+    taps = torch.nn.functional.pad(taps, (0, 0, 0, 0, 0, rows - out_channels))
+    flat = taps.reshape(parities, rows, ntaps * cpad)
+    packed = _split_planes(flat) if exact else flat.to(torch.float16)
+    return packed.reshape(parities * rows, -1).contiguous()
+
+
+def pack_weight(weight: torch.Tensor, *, stride: int = 1) -> PackedWeight:
+    """Pack a Torch ``(O, C, k, k, k)`` weight (k = 3 or 1) for the conv kernel.
+
+    Mirrors ``pack_weight`` (_nax_conv.py:350-364): input channels are
+    zero-padded to a multiple of 16; an FP32 weight packs for exact mode.
+    """
+    if weight.ndim != 5 or weight.shape[2] != weight.shape[3] or weight.shape[3] != weight.shape[4]:
+        raise ValueError(f"expected an (O, C, k, k, k) weight, got {tuple(weight.shape)}")
+    exact = weight.dtype == torch.float32
+    out_channels, in_channels, k = (int(s) for s in weight.shape[:3])
+    if k not in (1, 3):
+        raise ValueError("only 1x1x1 and 3x3x3 weights are supported")
+    kind = "pointwise" if k == 1 else "conv"
+    mode = MODE_POINTWISE if k == 1 else (MODE_STRIDE2 if stride == 2 else MODE_CONV)
+    rows, _ = _geometry(in_channels, out_channels, mode, exact)
+    cpad = (in_channels + 15) // 16 * 16
+    w = weight.detach().to(torch.float32)
+    taps = w.permute(0, 2, 3, 4, 1).reshape(out_channels, k ** 3, in_channels)
+    taps = torch.nn.functional.pad(taps, (0, cpad - in_channels))
+    return PackedWeight(_pack_rows(taps[None], rows, exact), kind, in_channels, out_channels, exact)
+
+
+def pack_dense_weight(weight: torch.Tensor) -> PackedWeight:
+    """Pack a ``(O, C)`` dense/linear weight as a pointwise conv."""
+    if weight.ndim != 2:
+        raise ValueError(f"expected an (O, C) weight, got {tuple(weight.shape)}")
+    return pack_weight(weight[:, :, None, None, None])
+
+
+def pack_upsample_weight(weight: torch.Tensor) -> PackedWeight:
+    """Fold a ``(O, C, 3, 3, 3)`` weight into eight 2x2x2 parity filters.
+
+    Same fold as ``pack_upsample_weight`` (_nax_conv.py:367-405): per axis,
+    parity 0 uses taps (k0, k1 + k2) on source offsets (m - 1, m) and parity 1
+    uses (k0 + k1, k2) on (m, m + 1).  Sums are FP32, folded axis by axis, and
+    rounded to f16 once (FP32 weights keep the sums and split into planes).
+    """
+    if weight.ndim != 5 or tuple(weight.shape[2:]) != (3, 3, 3):
+        raise ValueError(f"expected an (O, C, 3, 3, 3) weight, got {tuple(weight.shape)}")
+    exact = weight.dtype == torch.float32
+    out_channels, in_channels = int(weight.shape[0]), int(weight.shape[1])
+    rows, _ = _geometry(in_channels, out_channels, MODE_UP2, exact)
+    cpad = (in_channels + 15) // 16 * 16
+    w = weight.detach().to(torch.float32)
+
+    def fold(t: torch.Tensor, dim: int) -> torch.Tensor:
+        k0, k1, k2 = t.unbind(dim)
+        return torch.stack([torch.stack([k0, k1 + k2], dim), torch.stack([k0 + k1, k2], dim)], dim)
+
+    f = fold(w, 2)        # (O, C, pd, td, kh, kw)
+    f = fold(f, 4)        # (O, C, pd, td, ph, th, kw)
+    f = fold(f, 6)        # (O, C, pd, td, ph, th, pw, tw)
+    f = f.permute(2, 4, 6, 0, 3, 5, 7, 1)  # (pd, ph, pw, O, td, th, tw, C)
+    f = f.reshape(8, out_channels, 8, in_channels)
+    f = torch.nn.functional.pad(f, (0, cpad - in_channels))
+    return PackedWeight(_pack_rows(f, rows, exact), "up", in_channels, out_channels, exact)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def conv3d_ndhwc(
+    x: torch.Tensor,
+    packed: PackedWeight,
+    bias: torch.Tensor | None = None,
+    *,
+    stride: int = 1,
+    shift: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    output_scale: float = 1.0,
+    act: int = _lib.LDB_ACT_NONE,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype | None = None,
+    in_channels: int | None = None,
+) -> torch.Tensor:
+    """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = last-dim stride).
+
+    ``x`` is f16 (or, for exact weights, the split hi/lo f16 planes from
+    ``prepare_input``).  ``bias`` is f32 ``(O,)``; ``shift`` f32 ``(B, O)``;
+    ``residual`` has the output's dtype and shape.  The output is NDHWC with
+    ``O`` channels (a caller-supplied ``out`` may be a channel slice of a
+    wider buffer).  Stride applies only to ``kind == "conv"`` weights.
+    """
+    if x.device.type != "cuda":
+        raise ValueError("conv3d_ndhwc needs CUDA tensors")
+    if x.dtype != torch.float16:
+        raise ValueError(f"conv input must be float16 (split planes for FP32), got {x.dtype}")
+    if x.ndim != 5 or x.stride(4) != 1:
+        raise ValueError("x must be (B, D, H, W, C) with unit channel stride")
+    batch, depth, height, width = (int(s) for s in x.shape[:4])
+    x_ld = int(x.stride(3))
+    if x.stride(2) != width * x_ld or x.stride(1) != height * width * x_ld or x.stride(0) != depth * height * width * x_ld:
+        raise ValueError("x must be dense over voxels (only the channel stride may exceed C)")
+    cin = packed.in_channels if in_channels is None else in_channels
+    if packed.kind == "up":
+        mode = MODE_UP2
+        if stride != 1:
+            raise ValueError("upsampling convolution has stride 1")
+        grid = (2 * depth, 2 * height, 2 * width)
+    elif packed.kind == "pointwise":
+        mode = MODE_POINTWISE
+        grid = (depth, height, width)
+    else:
+        mode = MODE_STRIDE2 if stride == 2 else MODE_CONV
+        grid = (depth, height, width) if stride == 1 else tuple((n - 1) // 2 + 1 for n in (depth, height, width))
+    cout = packed.out_channels
+    if out_dtype is None:
+        out_dtype = torch.float32 if packed.exact else torch.float16
+    if out is None:
+        out = torch.empty((batch, *grid, cout), device=x.device, dtype=out_dtype)
+    if out.dtype != out_dtype or tuple(out.shape) != (batch, *grid, cout) or out.stride(4) != 1:
+        raise ValueError(f"out must be {(batch, *grid, cout)} {out_dtype} with unit channel stride")
+    res_ld = cout
+    if residual is not None:
+        if tuple(residual.shape) != (batch, *grid, cout) or residual.dtype != out_dtype or residual.stride(4) != 1:
+            raise ValueError(f"residual shape {tuple(residual.shape)} {residual.dtype} != output {(batch, *grid, cout)} {out_dtype}")
+        res_ld = int(residual.stride(3))
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != cout or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous float32 (O,) tensor")
+    if shift is not None and (shift.dtype != torch.float32 or tuple(shift.shape) != (batch, cout) or not shift.is_contiguous()):
+        raise ValueError("shift must be a contiguous float32 (B, O) tensor")
+    desc = _lib.ConvDesc(
+        batch=batch, depth=depth, height=height, width=width, in_channels=cin, x_ld=x_ld,
+        out_channels=cout, out_ld=int(out.stride(3)), res_ld=res_ld, mode=mode, exact=int(packed.exact),
+        out_dtype=_lib.LDB_F32 if out_dtype == torch.float32 else _lib.LDB_F16, act=act,
+        output_scale=float(output_scale),
+    )
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(ws_bytes))
+    workspace = None
+    if ws_bytes.value:
+        workspace = torch.empty(ws_bytes.value, dtype=torch.uint8, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _lib.call(
+        "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
+        _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,
+    )
+    return out

@@ -1,0 +1,691 @@
+// Implicit-GEMM 3-D convolution on sm_100a tensor cores (tcgen05 + TMEM).
+//
+// GEMM view: rows M are output voxels (source voxels for the folded 2x
+// upsampling conv), columns N are output channels, and K runs over
+// (tap, input-channel block).  Nothing is im2col'ed: for each K block the
+// producer warp issues one 5-D TMA load of a bd x bh x bw brick of voxels x
+// KC channels of the NDHWC activation, offset by the tap; TMA's out-of-bounds
+// zero fill supplies the padding.  Weights are packed K-major
+// [parity][Cout][tap][Cin] and loaded as 2-D TMA tiles.  A single thread of
+// the MMA warp issues tcgen05.mma (M=128, N=BN, K=16) into a double-buffered
+// TMEM accumulator; four epilogue warps drain TMEM (tcgen05.ld), add bias,
+// per-batch shift, output scale, residual, optional GELU, round once and
+// store NDHWC.  The kernel is persistent: CTA i walks tiles i, i+grid, ...
+//
+// FP32 "exact" mode follows the reference's split (hi = f16(v), lo =
+// f16((v - hi) * 2^11)): per K step it issues hi*hi into one accumulator and
+// hi*lo + lo*hi into a second, combined as acc0 + acc1 / 2048 in the
+// epilogue, as in lesiondiffusion_mlx/_nax_conv.py:26-34 and :224-235.
+//
+// Split-K: when the output has too few tiles to fill the GPU, K is split
+// into ranges computed by different CTAs; each stores raw f32 partial tiles
+// and conv_reduce_kernel sums them and applies the epilogue, mirroring the
+// reference's SPLIT/reduce kernels (_nax_conv.py:277-289, :556-563).
+
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "conv3d.cuh"
+#include "host_common.h"
+
+namespace ldb {
+
+namespace {
+
+constexpr int kConvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTileM = 128;
+
+struct TileCoord {
+  int b, td, th, tw, par, nt, ks, out_tile;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const ConvParams& p, int t) {
+  TileCoord c;
+  c.ks = t % p.k_splits;
+  t /= p.k_splits;
+  c.out_tile = t;
+  c.nt = t % p.n_tiles;
+  t /= p.n_tiles;
+  c.par = t % p.parities;
+  t /= p.parities;
+  c.tw = t % p.tiles_w;
+  t /= p.tiles_w;
+  c.th = t % p.tiles_h;
+  t /= p.tiles_h;
+  c.td = t % p.tiles_d;
+  c.b = t / p.tiles_d;
+  return c;
+}
+
+// Output voxel (linear NDHW index) of GEMM row `r` of a tile, or -1 when
+// the row falls outside the brick or the volume.
+__device__ __forceinline__ long long row_voxel(const ConvParams& p, const TileCoord& c, int r) {
+  const int brick = p.bw * p.bh * p.bd;
+  if (r >= brick) return -1;
+  const int lw = r % p.bw;
+  const int lh = (r / p.bw) % p.bh;
+  const int ld = r / (p.bw * p.bh);
+  int w = c.tw * p.bw + lw;
+  int h = c.th * p.bh + lh;
+  int d = c.td * p.bd + ld;
+  if (w >= p.grid_w || h >= p.grid_h || d >= p.grid_d) return -1;
+  if (p.mode == kConvUp2) {
+    d = 2 * d + (c.par >> 2);
+    h = 2 * h + ((c.par >> 1) & 1);
+    w = 2 * w + (c.par & 1);
+  }
+  return ((static_cast<long long>(c.b) * p.out_d + d) * p.out_h + h) * p.out_w + w;
+}
+
+// Apply the epilogue to `n` consecutive output channels starting at `col`
+// of one voxel and store them.  `v` holds the f32 GEMM sums.
+template <int N>
+__device__ __forceinline__ void store_outputs(const ConvParams& p, int b, long long voxel, int col, float (&v)[N]) {
+  const bool full = (col + N <= p.cout);
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const int c = col + j;
+    float y = v[j];
+    if (c < p.cout) {
+      float add = p.bias ? p.bias[c] : 0.0f;
+      if (p.shift) add += p.shift[static_cast<long long>(b) * p.cout + c];
+      y = (y + add) * p.out_scale;
+    }
+    v[j] = y;
+  }
+  if (p.residual) {
+    if (p.out_f32) {
+      const float* res = static_cast<const float*>(p.residual) + voxel * p.res_ld + col;
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (col + j < p.cout) v[j] += res[j];
+    } else {
+      const __half* res = static_cast<const __half*>(p.residual) + voxel * p.res_ld + col;
+      if (full && (p.res_ld % 8) == 0 && (col % 8) == 0 && (N % 8) == 0) {
+#pragma unroll
+        for (int j = 0; j < N; j += 8) {
+          uint4 raw = *reinterpret_cast<const uint4*>(res + j);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float2 f = __half22float2(h2[q]);
+            v[j + 2 * q] += f.x;
+            v[j + 2 * q + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+          if (col + j < p.cout) v[j] += __half2float(res[j]);
+      }
+    }
+  }
+  if (p.act == kActGelu) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      // The reference rounds the dense output to the activation dtype before
+      // its FP32 GELU (mlx_model.py:369-374 after :204-217).
+      float y = p.out_f32 ? v[j] : __half2float(__float2half_rn(v[j]));
+      v[j] = gelu_erf_f32(y);
+    }
+  }
+  if (p.out_f32) {
+    float* o = static_cast<float*>(p.out) + voxel * p.out_ld + col;
+    if (full && (p.out_ld % 4) == 0 && (col % 4) == 0 && (N % 4) == 0) {
+#pragma unroll
+      for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (col + j < p.cout) o[j] = v[j];
+    }
+  } else {
+    __half* o = static_cast<__half*>(p.out) + voxel * p.out_ld + col;
+    if (full && (p.out_ld % 8) == 0 && (col % 8) == 0 && (N % 8) == 0) {
+#pragma unroll
+      for (int j = 0; j < N; j += 8) {
+        uint4 raw;
+        __half2* h2 = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) h2[q] = __floats2half2_rn(v[j + 2 * q], v[j + 2 * q + 1]);
+        *reinterpret_cast<uint4*>(o + j) = raw;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (col + j < p.cout) o[j] = __float2half_rn(v[j]);
+    }
+  }
+}
+
+template <int KC, int BN, bool EXACT>
+struct ConvCfg {
+  static constexpr int kSwizzleBytes = KC * 2;  // one K block row = 32/64/128 B
+  static constexpr uint32_t kLayout = KC == 64 ? kSwizzle128 : (KC == 32 ? kSwizzle64 : kSwizzle32);
+  static constexpr uint32_t kSbo = 8 * KC * 2;  // bytes between 8-row groups
+  static constexpr int kPlanes = EXACT ? 2 : 1;
+  static constexpr int kABytes = kTileM * KC * 2;
+  static constexpr int kBBytesRaw = BN * KC * 2;
+  static constexpr int kBBytes = ((kBBytesRaw + 1023) / 1024) * 1024;
+  static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
+  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kAccCols = BN * kPlanes;
+  static constexpr int kTmemColsRaw = 2 * kAccCols;
+  static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
+  static constexpr int kChunk = BN < 32 ? BN : 32;
+  static constexpr uint32_t kIdesc = make_idesc_f16(kTileM, BN, 0, 0, 0);
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain
+  static constexpr int kBarrierBytes = (2 * kStages + 5) * 8;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + kBarrierBytes + 64;
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+};
+
+template <int KC, int BN, bool EXACT>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    conv3d_tc_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ CUtensorMap wmap,
+                     const ConvParams p, unsigned int* status) {
+  using Cfg = ConvCfg<KC, BN, EXACT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* acc_full = empty + Cfg::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&wmap);
+    const int nmaps = p.mode == kConv3x3x3S2 ? 8 : 1;
+    for (int i = 0; i < nmaps; ++i) tma_prefetch_desc(&maps.a[i]);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const uint32_t a_box_bytes = static_cast<uint32_t>(KC * 2 * p.bw * p.bh * p.bd);
+  const uint32_t tx_bytes = Cfg::kPlanes * (a_box_bytes + static_cast<uint32_t>(Cfg::kBBytesRaw));
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_mask = 0, armed_parity = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+        const TileCoord c = decode_tile(p, t);
+        const int kb0 = c.ks * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
+        const int pd = c.par >> 2, ph = (c.par >> 1) & 1, pw = c.par & 1;
+        const int brow = c.par * p.wrows_per_parity + c.nt * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kPlanes * Cfg::kABytes;
+          mbar_arrive_expect_tx(&full[stage], tx_bytes);
+          armed_mask |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          const int tap = kb / p.cin_chunks;
+          const int chn = (kb - tap * p.cin_chunks) * KC;
+          int map = 0, x = w0, y = h0, z = d0;
+          if (p.mode == kConv3x3x3) {
+            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            x = w0 + kw - 1;
+            y = h0 + kh - 1;
+            z = d0 + kd - 1;
+          } else if (p.mode == kConv3x3x3S2) {
+            // input index 2o + k - 1: k = 1 -> parity 0 at o; k = 0 -> parity 1
+            // at o - 1; k = 2 -> parity 1 at o.
+            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            map = (kd != 1) * 4 + (kh != 1) * 2 + (kw != 1);
+            x = w0 - (kw == 0);
+            y = h0 - (kh == 0);
+            z = d0 - (kd == 0);
+          } else if (p.mode == kConvUp2) {
+            // parity p, folded tap t reads source index m + p + t - 1.
+            const int td = tap >> 2, th = (tap >> 1) & 1, tw = tap & 1;
+            x = w0 + pw + tw - 1;
+            y = h0 + ph + th - 1;
+            z = d0 + pd + td - 1;
+          }
+          tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
+          tma_load_2d(sb, &wmap, &full[stage], tap * p.cin_pad + chn, brow);
+          if (EXACT) {
+            tma_load_5d(sa + Cfg::kABytes, &maps.a[map], &full[stage], p.cin_pad + chn, x, y, z, c.b);
+            tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + tap * p.cin_pad + chn, brow);
+          }
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // Let every armed TMA land before the CTA releases its shared memory.
+        volatile int never = 0;
+        for (int s = 0; s < Cfg::kStages; ++s)
+          if (armed_mask & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never, status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++local) {
+        const TileCoord c = decode_tile(p, t);
+        const int kb0 = c.ks * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const int acc = local & 1;
+        if (!mbar_wait(&acc_empty[acc], ((local >> 1) & 1) ^ 1u, abort_flag, status)) break;
+        tc_fence_after();
+        const uint32_t d_hi = tmem_base + acc * Cfg::kAccCols;
+        const uint32_t d_lo = d_hi + BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t b_addr = a_addr + Cfg::kPlanes * Cfg::kABytes;
+#pragma unroll
+          for (int k = 0; k < KC / 16; ++k) {
+            const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+            const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            umma_ss(d_hi, ad, bd, Cfg::kIdesc, accum);
+            if (EXACT) {
+              const uint64_t ad_lo = make_smem_desc(a_addr + Cfg::kABytes + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+              const uint64_t bd_lo = make_smem_desc(b_addr + Cfg::kBBytes + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+              umma_ss(d_lo, ad, bd_lo, Cfg::kIdesc, accum);
+              umma_ss(d_lo, ad_lo, bd, Cfg::kIdesc, 1u);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+      }
+      // All issued MMAs must finish before TMEM is released.
+      umma_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never, status);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const TileCoord c = decode_tile(p, t);
+      const int acc = local & 1;
+      if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, abort_flag, status)) break;
+      tc_fence_after();
+      const long long voxel = row_voxel(p, c, row);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * Cfg::kAccCols;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += Cfg::kChunk) {
+        float v[Cfg::kChunk];
+        {
+          uint32_t r[Cfg::kChunk];
+          if constexpr (Cfg::kChunk == 32) tmem_ld32(tbase + c0, r);
+          else tmem_ld16(tbase + c0, r);
+          if constexpr (EXACT) {
+            uint32_t q[Cfg::kChunk];
+            if constexpr (Cfg::kChunk == 32) tmem_ld32(tbase + BN + c0, q);
+            else tmem_ld16(tbase + BN + c0, q);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < Cfg::kChunk; ++j)
+              v[j] = __uint_as_float(r[j]) + __uint_as_float(q[j]) * (1.0f / 2048.0f);
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < Cfg::kChunk; ++j) v[j] = __uint_as_float(r[j]);
+          }
+        }
+        const int col = c.nt * BN + c0;
+        if (p.k_splits > 1) {
+          float* dst = p.partials + ((static_cast<long long>(c.ks) * (p.num_tiles / p.k_splits) + c.out_tile) * kTileM + row) * BN + c0;
+#pragma unroll
+          for (int j = 0; j < Cfg::kChunk; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else if (voxel >= 0 && col < p.cout) {
+          store_outputs<Cfg::kChunk>(p, c.b, voxel, col, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// Sum split-K partial tiles and apply the epilogue: one thread per 4 columns
+// of one row of one output tile.
+template <int BN>
+__global__ void conv_reduce_kernel(const ConvParams p) {
+  const int out_tiles = p.num_tiles / p.k_splits;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(out_tiles) * kTileM * (BN / 4);
+  if (idx >= total) return;
+  const int q = static_cast<int>(idx % (BN / 4));
+  const int row = static_cast<int>((idx / (BN / 4)) % kTileM);
+  const int ot = static_cast<int>(idx / (static_cast<long long>(BN / 4) * kTileM));
+  const TileCoord c = decode_tile(p, ot * p.k_splits);
+  const long long voxel = row_voxel(p, c, row);
+  const int col = c.nt * BN + q * 4;
+  if (voxel < 0 || col >= p.cout) return;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < p.k_splits; ++s) {
+    const float4 f = *reinterpret_cast<const float4*>(
+        p.partials + ((static_cast<long long>(s) * out_tiles + ot) * kTileM + row) * BN + q * 4);
+    v[0] += f.x;
+    v[1] += f.y;
+    v[2] += f.z;
+    v[3] += f.w;
+  }
+  store_outputs<4>(p, c.b, voxel, col, v);
+}
+
+// Brick of at most 128 voxels covering a (d, h, w) grid with the fewest
+// tiles; ties prefer wider bricks (longer contiguous TMA rows, more
+// coalesced stores).
+void choose_brick(int d, int h, int w, bool pointwise, int* bd, int* bh, int* bw) {
+  long best_tiles = -1;
+  int best[3] = {1, 1, 1};
+  const int max_w = std::min(w, 128);
+  for (int cw = max_w; cw >= 1; --cw) {
+    const int max_h = std::min(h, 128 / cw);
+    for (int ch = max_h; ch >= 1; --ch) {
+      const int cd = std::min(d, 128 / (cw * ch));
+      if (cd < 1) continue;
+      const long tiles = static_cast<long>((w + cw - 1) / cw) * ((h + ch - 1) / ch) * ((d + cd - 1) / cd);
+      if (best_tiles < 0 || tiles < best_tiles) {
+        best_tiles = tiles;
+        best[0] = cd;
+        best[1] = ch;
+        best[2] = cw;
+      }
+    }
+    if (pointwise && best_tiles > 0) break;
+  }
+  *bd = best[0];
+  *bh = best[1];
+  *bw = best[2];
+}
+
+template <int KC, int BN, bool EXACT>
+int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wmap, const ConvParams& p,
+                int grid) {
+  using Cfg = ConvCfg<KC, BN, EXACT>;
+  auto kernel = conv3d_tc_kernel<KC, BN, EXACT>;
+  int smem = Cfg::kSmemBytes;
+  // Keep one CTA per SM when the accumulators need more than half of TMEM,
+  // so co-resident CTAs never queue on tcgen05.alloc.
+  if (Cfg::kTmemCols > 256 && smem < 120 * 1024) smem = 120 * 1024;
+  static bool configured = false;
+  if (!configured) {
+    int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                        "conv smem attribute");
+    if (rc != LDB_OK) return rc;
+    configured = true;
+  }
+  kernel<<<grid, kConvThreads, smem, stream>>>(maps, wmap, p, device_status_ptr());
+  int rc = check_cuda(cudaGetLastError(), "conv3d launch");
+  if (rc != LDB_OK) return rc;
+  if (p.k_splits > 1) {
+    const long long total = static_cast<long long>(p.num_tiles / p.k_splits) * kTileM * (BN / 4);
+    const int threads = 256;
+    conv_reduce_kernel<BN><<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(p);
+    rc = check_cuda(cudaGetLastError(), "conv3d split-K reduce launch");
+  }
+  return rc;
+}
+
+template <int KC, bool EXACT>
+int dispatch_bn(int bn, cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wmap, const ConvParams& p,
+                int grid) {
+  switch (bn) {
+    case 16: return launch_conv<KC, 16, EXACT>(stream, maps, wmap, p, grid);
+    case 32: return launch_conv<KC, 32, EXACT>(stream, maps, wmap, p, grid);
+    case 64: return launch_conv<KC, 64, EXACT>(stream, maps, wmap, p, grid);
+    case 128: return launch_conv<KC, 128, EXACT>(stream, maps, wmap, p, grid);
+    case 256:
+      if constexpr (!EXACT) return launch_conv<KC, 256, false>(stream, maps, wmap, p, grid);
+      break;
+  }
+  return fail(LDB_ERR_SHAPE, "no conv kernel for BN=%d", bn);
+}
+
+struct ConvPlan {
+  int kc, bn, taps, cin_pad, grid;
+  ConvParams p;
+  size_t workspace;
+};
+
+int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
+  if (!d) return fail(LDB_ERR_INVALID, "conv descriptor is null");
+  const int B = d->batch, D = d->depth, H = d->height, W = d->width;
+  if (B <= 0 || D <= 0 || H <= 0 || W <= 0) return fail(LDB_ERR_SHAPE, "conv input extents must be positive");
+  if (d->in_channels <= 0 || d->out_channels <= 0) return fail(LDB_ERR_SHAPE, "conv channels must be positive");
+  if (d->mode < 0 || d->mode > 3) return fail(LDB_ERR_INVALID, "unknown conv mode %d", d->mode);
+  const bool exact = d->exact != 0;
+  const int cin = d->in_channels;
+  const int cin_pad = ((cin + 15) / 16) * 16;
+  const int kc = (cin_pad % 64 == 0) ? 64 : ((cin_pad % 32 == 0) ? 32 : 16);
+  const int cout = d->out_channels;
+  if (cout % 4 != 0 && cout != 1 && cout != 2) {
+    // every column count works; the vector paths simply fall back to scalar stores
+  }
+  const int need_ld = exact ? 2 * cin_pad : cin;
+  if (d->x_ld < need_ld) return fail(LDB_ERR_SHAPE, "x_ld %d < %d channels", d->x_ld, need_ld);
+  if (d->x_ld % 8 != 0) return fail(LDB_ERR_ALIGNMENT, "x_ld %d must be a multiple of 8", d->x_ld);
+  if (d->out_ld < cout) return fail(LDB_ERR_SHAPE, "out_ld %d < out_channels %d", d->out_ld, cout);
+  int bn;
+  if (cout <= 16) bn = 16;
+  else if (cout <= 32) bn = 32;
+  else if (cout <= 64) bn = 64;
+  else if (cout <= 128 || exact) bn = 128;
+  else bn = 256;
+  ConvParams& p = plan->p;
+  p = ConvParams{};
+  p.batch = B;
+  p.mode = d->mode;
+  int gd = D, gh = H, gw = W;
+  if (d->mode == LDB_CONV_3X3X3_S2) {
+    gd = (D - 1) / 2 + 1;
+    gh = (H - 1) / 2 + 1;
+    gw = (W - 1) / 2 + 1;
+  }
+  p.grid_d = gd;
+  p.grid_h = gh;
+  p.grid_w = gw;
+  choose_brick(gd, gh, gw, d->mode == LDB_CONV_1X1, &p.bd, &p.bh, &p.bw);
+  p.tiles_d = (gd + p.bd - 1) / p.bd;
+  p.tiles_h = (gh + p.bh - 1) / p.bh;
+  p.tiles_w = (gw + p.bw - 1) / p.bw;
+  p.parities = d->mode == LDB_CONV_UP2 ? 8 : 1;
+  const int taps = d->mode == LDB_CONV_1X1 ? 1 : (d->mode == LDB_CONV_UP2 ? 8 : 27);
+  p.taps = taps;
+  p.cin_pad = cin_pad;
+  p.cin_chunks = cin_pad / kc;
+  p.kb_total = taps * p.cin_chunks;
+  p.n_tiles = (cout + bn - 1) / bn;
+  p.wrows_per_parity = p.n_tiles * bn;
+  const long long out_tiles =
+      static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
+  if (out_tiles > (1LL << 30)) return fail(LDB_ERR_SHAPE, "conv has too many tiles");
+  const int sms = sm_count();
+  int splits = 1;
+  if (out_tiles < sms && p.kb_total >= 8) {
+    splits = static_cast<int>(std::min<long long>(sms / out_tiles, p.kb_total / 4));
+    splits = std::max(1, splits);
+  }
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  p.num_tiles = static_cast<int>(out_tiles * p.k_splits);
+  p.cout = cout;
+  p.out_ld = d->out_ld;
+  p.res_ld = d->res_ld;
+  p.out_f32 = d->out_dtype == LDB_F32 ? 1 : 0;
+  p.out_scale = d->output_scale;
+  p.act = d->act;
+  const int up = d->mode == LDB_CONV_UP2 ? 2 : 1;
+  p.out_d = gd * up;
+  p.out_h = gh * up;
+  p.out_w = gw * up;
+  plan->kc = kc;
+  plan->bn = bn;
+  plan->taps = taps;
+  plan->cin_pad = cin_pad;
+  plan->grid = static_cast<int>(std::min<long long>(p.num_tiles, sms));
+  plan->workspace = p.k_splits > 1 ? static_cast<size_t>(p.num_tiles) * kTileM * bn * sizeof(float) : 0;
+  return LDB_OK;
+}
+
+}  // namespace
+
+}  // namespace ldb
+
+extern "C" {
+
+int ldb_conv3d_workspace_size(const ldb_conv_desc* desc, size_t* bytes) {
+  if (!bytes) return ldb::fail(LDB_ERR_INVALID, "bytes pointer is null");
+  ldb::ConvPlan plan;
+  int rc = ldb::plan_conv(desc, &plan);
+  if (rc != LDB_OK) return rc;
+  *bytes = plan.workspace;
+  return LDB_OK;
+}
+
+int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_parity, int* k_total) {
+  ldb::ConvPlan plan;
+  int rc = ldb::plan_conv(desc, &plan);
+  if (rc != LDB_OK) return rc;
+  if (rows_per_parity) *rows_per_parity = plan.p.wrows_per_parity;
+  if (k_total) *k_total = plan.taps * plan.cin_pad * (desc->exact ? 2 : 1);
+  return LDB_OK;
+}
+
+int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
+                   const float* bias, const float* shift, const void* residual, void* out, void* workspace,
+                   size_t workspace_bytes) {
+  using namespace ldb;
+  ConvPlan plan;
+  int rc = plan_conv(desc, &plan);
+  if (rc != LDB_OK) return rc;
+  if (!x || !w_packed || !out) return fail(LDB_ERR_INVALID, "conv3d: x, weights and out must be non-null");
+  if (residual && desc->res_ld < desc->out_channels)
+    return fail(LDB_ERR_SHAPE, "res_ld %d < out_channels %d", desc->res_ld, desc->out_channels);
+  if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
+    return fail(LDB_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", plan.workspace, workspace_bytes);
+  ConvParams& p = plan.p;
+  p.bias = bias;
+  p.shift = shift;
+  p.residual = residual;
+  p.out = out;
+  p.partials = static_cast<float*>(workspace);
+
+  const int B = desc->batch, D = desc->depth, H = desc->height, W = desc->width;
+  const bool exact = desc->exact != 0;
+  const uint64_t esz = 2;
+  const uint64_t ld = static_cast<uint64_t>(desc->x_ld);
+  const uint64_t cdim = exact ? 2 * plan.cin_pad : desc->in_channels;
+  ConvMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const uint32_t abox[5] = {static_cast<uint32_t>(plan.kc), static_cast<uint32_t>(p.bw),
+                            static_cast<uint32_t>(p.bh), static_cast<uint32_t>(p.bd), 1u};
+  if (desc->mode == LDB_CONV_3X3X3_S2) {
+    for (int par = 0; par < 8; ++par) {
+      const int pd = par >> 2, ph = (par >> 1) & 1, pw = par & 1;
+      const uint64_t dims[5] = {cdim, static_cast<uint64_t>((W - pw + 1) / 2), static_cast<uint64_t>((H - ph + 1) / 2),
+                                static_cast<uint64_t>((D - pd + 1) / 2), static_cast<uint64_t>(B)};
+      const uint64_t strides[4] = {2 * ld * esz, 2 * W * ld * esz, 2 * H * W * ld * esz,
+                                   static_cast<uint64_t>(D) * H * W * ld * esz};
+      if (dims[1] == 0 || dims[2] == 0 || dims[3] == 0) {
+        // A parity view with no voxels (extent 1): alias the even view; every
+        // coordinate it would serve is out of range and zero-filled anyway.
+        maps.a[par] = maps.a[0];
+        continue;
+      }
+      const uint8_t* base = static_cast<const uint8_t*>(x) +
+                            ((static_cast<uint64_t>(pd) * H + ph) * W + pw) * ld * esz;
+      rc = encode_tiled_f16(&maps.a[par], base, 5, dims, strides, abox, plan.kc * 2);
+      if (rc != LDB_OK) return rc;
+    }
+  } else {
+    const uint64_t dims[5] = {cdim, static_cast<uint64_t>(W), static_cast<uint64_t>(H), static_cast<uint64_t>(D),
+                              static_cast<uint64_t>(B)};
+    const uint64_t strides[4] = {ld * esz, W * ld * esz, static_cast<uint64_t>(H) * W * ld * esz,
+                                 static_cast<uint64_t>(D) * H * W * ld * esz};
+    rc = encode_tiled_f16(&maps.a[0], x, 5, dims, strides, abox, plan.kc * 2);
+    if (rc != LDB_OK) return rc;
+  }
+  CUtensorMap wmap;
+  const uint64_t ktotal = static_cast<uint64_t>(plan.taps) * plan.cin_pad * (exact ? 2 : 1);
+  const uint64_t wrows = static_cast<uint64_t>(p.parities) * p.wrows_per_parity;
+  const uint64_t wdims[2] = {ktotal, wrows};
+  const uint64_t wstrides[1] = {ktotal * esz};
+  const uint32_t wbox[2] = {static_cast<uint32_t>(plan.kc), static_cast<uint32_t>(plan.bn)};
+  rc = encode_tiled_f16(&wmap, w_packed, 2, wdims, wstrides, wbox, plan.kc * 2);
+  if (rc != LDB_OK) return rc;
+
+  switch (plan.kc) {
+    case 16:
+      return exact ? dispatch_bn<16, true>(plan.bn, stream, maps, wmap, p, plan.grid)
+                   : dispatch_bn<16, false>(plan.bn, stream, maps, wmap, p, plan.grid);
+    case 32:
+      return exact ? dispatch_bn<32, true>(plan.bn, stream, maps, wmap, p, plan.grid)
+                   : dispatch_bn<32, false>(plan.bn, stream, maps, wmap, p, plan.grid);
+    default:
+      return exact ? dispatch_bn<64, true>(plan.bn, stream, maps, wmap, p, plan.grid)
+                   : dispatch_bn<64, false>(plan.bn, stream, maps, wmap, p, plan.grid);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,39 @@
+// Host-side helpers shared by the C-ABI entry points: status codes, the
+// thread-local error string, tensor-map encoding through the driver entry
+// point, and per-device properties.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/ldb200.h"
+
+namespace ldb {
+
+void set_last_error(const char* fmt, ...);
+
+// Return `code` after recording a formatted message for ldb_last_error().
+int fail(int code, const char* fmt, ...);
+
+// Map a CUDA runtime error to LDB_ERR_CUDA (recording its text), or LDB_OK.
+int check_cuda(cudaError_t err, const char* what);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Device address of the current device's status word (cached per device).
+unsigned int* device_status_ptr();
+
+// Encode a tiled tensor map with 16-bit elements.  `dims`/`box` are
+// innermost first; `strides_bytes` has rank-1 entries (dims 1..rank-1).
+// swizzle_bytes is 0, 32, 64 or 128.  Returns LDB_OK or an error code.
+int encode_tiled_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes,
+                     bool bf16 = false);
+
+}  // namespace ldb
