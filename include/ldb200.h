@@ -62,6 +62,10 @@ enum { LDB_ACT_NONE = 0, LDB_ACT_GELU = 1 };
 /* Library ABI version (LDB_ABI_VERSION). */
 LDB_API int ldb_version(void);
 
+/* Number of kernels this library has launched (or recorded into a CUDA
+ * graph) in this process, for launch accounting in benchmarks. */
+LDB_API unsigned long long ldb_launch_count(void);
+
 /* Message describing the last failure on the calling thread. */
 LDB_API const char* ldb_last_error(void);
 
@@ -109,6 +113,99 @@ LDB_API int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_pari
 LDB_API int ldb_conv3d_fwd(ldb_stream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
                    const float* bias, const float* shift, const void* residual, void* out, void* workspace,
                    size_t workspace_bytes);
+
+/* -------------------------------------------------------------------------
+ * Group normalization: replaces medmlx-core's group_norm_affine (called at
+ * mlx_model.py:328-335 and _scaled_vq.py:93-100).  The input is the channel
+ * concatenation [x1 | x2] (c2 = 0 for a single tensor) of f16 or f32 NDHWC
+ * tensors with `voxels` voxels per batch item.  Writes the per-(batch,
+ * channel) FP32 affine (scale, offset) of GroupNorm(groups, eps, gamma,
+ * beta): affine[(b * C + c) * 2 + {0, 1}].  gamma/beta are f32 (null = 1/0).
+ * ---------------------------------------------------------------------- */
+LDB_API int ldb_group_norm_workspace_size(int batch, int voxels, int channels, size_t* bytes);
+LDB_API int ldb_group_norm_affine(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
+                                  int ld2, int dtype, int batch, int voxels, int groups, const float* gamma,
+                                  const float* beta, float eps, float* affine, void* workspace,
+                                  size_t workspace_bytes);
+
+/* Conv-input preparation: replaces the pack kernel of _nax_conv.py:109-155
+ * (and native_group_norm, mlx_model.py:348-358, when used with an affine).
+ * out = f16(silu?(x * scale + offset)) over [x1 | x2], or with split = 1 the
+ * exact-mode hi / 2^11-scaled lo planes (each padded to 16 channels).
+ * Channels are zero padded up to out_ld's plane width. */
+LDB_API int ldb_prepare_input(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
+                              int ld2, int dtype, int batch, int voxels, const float* affine, int silu, int split,
+                              void* out, int out_ld);
+
+/* LayerNorm over the last axis of f16 rows (mlx_model.py:360-367). */
+LDB_API int ldb_layer_norm(ldb_stream_t stream, const void* x, int x_ld, const float* gamma, const float* beta,
+                           float eps, void* out, int out_ld, int rows, int channels);
+
+/* -------------------------------------------------------------------------
+ * Attention: replaces flash_attention / flash_attention_half
+ * (_attention.py:331-375, _attention_half.py:129-147) and the fused SDPA
+ * cross-attention (mlx_model.py:477-487).  q (B, lq, q_ld), k/v (B, lk,
+ * kv_ld), out (B, lq, out_ld); head h uses columns [h*head_dim, (h+1)*head_dim).
+ * head_dim 16, 32 or 64, dtype LDB_F16 or LDB_BF16, any lq / lk.
+ * ---------------------------------------------------------------------- */
+LDB_API int ldb_flash_attention(ldb_stream_t stream, const void* q, int q_ld, const void* k, const void* v,
+                                int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim,
+                                float scale, int dtype);
+
+/* -------------------------------------------------------------------------
+ * Denoise-loop kernels.
+ * ---------------------------------------------------------------------- */
+
+/* Device-side step counter.  The denoise-step kernels below can read their
+ * per-step inputs (timesteps, sampler coefficients, noise) from device tables
+ * indexed by *step, so one captured CUDA graph of a step serves every step;
+ * ldb_step_advance increments the counter on the stream. */
+LDB_API int ldb_step_advance(ldb_stream_t stream, int* step);
+
+/* [cos, sin] timestep embedding (mlx_model.py:609-612); out (batch, channels).
+ * timesteps is a device table [steps][batch]; step (device, optional)
+ * selects the row (row 0 when null). */
+LDB_API int ldb_timestep_embedding(ldb_stream_t stream, const int* timesteps, const int* step, int batch,
+                                   int channels, void* out, int out_dtype);
+
+/* Skinny dense layer for 1..16 rows (time-embedding MLP and the residual
+ * blocks' embedding projections, mlx_model.py:434 and :614):
+ * out = silu_out?(silu_in?(x) @ w^T + bias), f16 x / w, f32 bias. */
+LDB_API int ldb_dense_small(ldb_stream_t stream, const void* x, int x_ld, const void* w, const float* bias, void* out,
+                            int out_ld, int rows, int n_out, int k, int in_silu, int out_silu, int out_dtype,
+                            int round_f16);
+
+/* Fused sampler step (DdimSampler / Dpmpp2mSampler steps,
+ * mlx_sampling.py:172-185, _dpm.py:320-333): kind 0 = compose only,
+ * 1 = DDIM update with coefficients (alpha, previous, sigma, sqrt(1 - alpha), 0),
+ * 2 = DPM++-2M update with (alpha, sigma, ratio, clean, history).
+ * coeff_table is a device table [steps][5], noise a device buffer whose
+ * step s starts at s * noise_step_stride; both are indexed by *step (0
+ * when step is null).  x is the f32 (B, voxels, channels) state, updated in
+ * place; with a mask the known region is re-imposed from `image`; net_in
+ * (optional) receives the next f16 network input [x | mask] (or
+ * [x | image]) with channel stride in_ld, zero padded. */
+LDB_API int ldb_sampler_step(ldb_stream_t stream, int kind, float* x, float* prev, const void* eps, int eps_ld,
+                             const float* noise, long long noise_step_stride, const float* mask,
+                             const float* image, int image_channels, void* net_in, int in_ld, int batch,
+                             int voxels, int channels, const float* coeff_table, const int* step);
+
+/* Nearest 4-channel codebook search with the straight-through quantize
+ * (nearest_codebook4, _vq.py:64-82; VqAutoencoder.quantize,
+ * mlx_model.py:742-803).  indices[p] gets the code; `quantized` (optional)
+ * gets z + (e - z) in the dtype with channel stride out_ld. */
+LDB_API int ldb_vq_nearest4(ldb_stream_t stream, const void* z, int z_ld, long long positions, const void* codebook,
+                            int entries, int dtype, int* indices, void* quantized, int out_ld);
+
+/* Nearest resize of NDHWC rows of `row_bytes` bytes (upsample_nearest2 and
+ * resize_nearest, _spatial.py:41-69). */
+LDB_API int ldb_resize_nearest(ldb_stream_t stream, const void* x, int batch, int in_d, int in_h, int in_w,
+                               int row_bytes, int x_row_stride, void* out, int out_d, int out_h, int out_w,
+                               int out_row_stride);
+
+/* Inverse CT map to HU of channel 0 of n voxels (piecewise_ct(inverse=True),
+ * mlx_pipeline.py:72-96). */
+LDB_API int ldb_hu_map(ldb_stream_t stream, const void* x, int dtype, int x_ld, long long n, float* out);
 
 #ifdef __cplusplus
 }

@@ -57,13 +57,26 @@ _SZ = ctypes.c_size_t
 # name -> (argtypes); every function returns int unless listed in _RESTYPES.
 SIGNATURES: dict[str, list] = {
     "ldb_version": [],
+    "ldb_launch_count": [],
     "ldb_last_error": [],
     "ldb_device_status": [ctypes.POINTER(ctypes.c_uint), _I],
     "ldb_conv3d_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_SZ)],
     "ldb_conv3d_weight_rows": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_I), ctypes.POINTER(_I)],
     "ldb_conv3d_fwd": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _SZ],
+    "ldb_group_norm_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
+    "ldb_group_norm_affine": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _SZ],
+    "ldb_prepare_input": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I],
+    "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
+    "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],
+    "ldb_step_advance": [_P, _P],
+    "ldb_timestep_embedding": [_P, _P, _P, _I, _I, _P, _I],
+    "ldb_dense_small": [_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I],
+    "ldb_sampler_step": [_P, _I, _P, _P, _P, _I, _P, ctypes.c_longlong, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P],
+    "ldb_vq_nearest4": [_P, _P, _I, ctypes.c_longlong, _P, _I, _I, _P, _P, _I],
+    "ldb_resize_nearest": [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _I, _I],
+    "ldb_hu_map": [_P, _P, _I, _I, ctypes.c_longlong, _P],
 }
-_RESTYPES = {"ldb_last_error": ctypes.c_char_p}
+_RESTYPES = {"ldb_last_error": ctypes.c_char_p, "ldb_launch_count": ctypes.c_ulonglong}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -95,6 +108,11 @@ def call(name: str, *args) -> int:
     if rc < 0:
         raise LdbError(name, rc, lib.ldb_last_error().decode(errors="replace"))
     return rc
+
+
+def launch_count() -> int:
+    """Kernels launched (or captured) by the library so far in this process."""
+    return int(library().ldb_launch_count())
 
 
 def device_status(reset: bool = True) -> int:

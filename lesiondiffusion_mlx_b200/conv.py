@@ -16,7 +16,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib
+from . import _lib, instrument
 
 MODE_CONV, MODE_STRIDE2, MODE_UP2, MODE_POINTWISE = (
     _lib.LDB_CONV_3X3X3,
@@ -143,6 +143,37 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def conv_geometry(x_shape, x_strides, packed: PackedWeight, *, stride: int = 1,
+                  in_channels: int | None = None) -> tuple[int, tuple[int, int, int], int, int]:
+    """Validate an NDHWC input layout for ``packed``; return (mode, output grid, x_ld, cin).
+
+    Pure host logic (no device access), shared by ``conv3d_ndhwc`` and the CPU tests.
+    """
+    if len(x_shape) != 5 or (x_strides[4] != 1 and x_shape[4] != 1):
+        raise ValueError("x must be (B, D, H, W, C) with unit channel stride")
+    depth, height, width = (int(s) for s in x_shape[1:4])
+    x_ld = int(x_strides[3])
+    expect = x_ld
+    for dim in (3, 2, 1, 0):
+        if int(x_shape[dim]) != 1 and int(x_strides[dim]) != expect:
+            raise ValueError("x must be dense over voxels (only the channel stride may exceed C)")
+        expect *= int(x_shape[dim])
+    cin = packed.in_channels if in_channels is None else in_channels
+    if packed.kind == "up":
+        if stride != 1:
+            raise ValueError("upsampling convolution has stride 1")
+        return MODE_UP2, (2 * depth, 2 * height, 2 * width), x_ld, cin
+    if packed.kind == "pointwise":
+        if stride != 1:
+            raise ValueError("pointwise convolution has stride 1")
+        return MODE_POINTWISE, (depth, height, width), x_ld, cin
+    if stride == 2:
+        return MODE_STRIDE2, tuple((n - 1) // 2 + 1 for n in (depth, height, width)), x_ld, cin
+    if stride != 1:
+        raise ValueError("stride must be 1 or 2")
+    return MODE_CONV, (depth, height, width), x_ld, cin
+
+
 def conv3d_ndhwc(
     x: torch.Tensor,
     packed: PackedWeight,
@@ -157,52 +188,42 @@ def conv3d_ndhwc(
     out_dtype: torch.dtype | None = None,
     in_channels: int | None = None,
 ) -> torch.Tensor:
-    """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = last-dim stride).
+    """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
     ``x`` is f16 (or, for exact weights, the split hi/lo f16 planes from
     ``prepare_input``).  ``bias`` is f32 ``(O,)``; ``shift`` f32 ``(B, O)``;
     ``residual`` has the output's dtype and shape.  The output is NDHWC with
-    ``O`` channels (a caller-supplied ``out`` may be a channel slice of a
-    wider buffer).  Stride applies only to ``kind == "conv"`` weights.
+    ``O`` channels; a new output has its channel stride padded to 8 so it can
+    feed the next convolution.  Stride applies only to ``kind == "conv"``.
     """
     if x.device.type != "cuda":
         raise ValueError("conv3d_ndhwc needs CUDA tensors")
     if x.dtype != torch.float16:
         raise ValueError(f"conv input must be float16 (split planes for FP32), got {x.dtype}")
-    if x.ndim != 5 or x.stride(4) != 1:
-        raise ValueError("x must be (B, D, H, W, C) with unit channel stride")
-    batch, depth, height, width = (int(s) for s in x.shape[:4])
-    x_ld = int(x.stride(3))
-    if x.stride(2) != width * x_ld or x.stride(1) != height * width * x_ld or x.stride(0) != depth * height * width * x_ld:
-        raise ValueError("x must be dense over voxels (only the channel stride may exceed C)")
-    cin = packed.in_channels if in_channels is None else in_channels
-    if packed.kind == "up":
-        mode = MODE_UP2
-        if stride != 1:
-            raise ValueError("upsampling convolution has stride 1")
-        grid = (2 * depth, 2 * height, 2 * width)
-    elif packed.kind == "pointwise":
-        mode = MODE_POINTWISE
-        grid = (depth, height, width)
-    else:
-        mode = MODE_STRIDE2 if stride == 2 else MODE_CONV
-        grid = (depth, height, width) if stride == 1 else tuple((n - 1) // 2 + 1 for n in (depth, height, width))
+    mode, grid, x_ld, cin = conv_geometry(tuple(x.shape), tuple(x.stride()), packed, stride=stride,
+                                          in_channels=in_channels)
+    batch = int(x.shape[0])
     cout = packed.out_channels
     if out_dtype is None:
         out_dtype = torch.float32 if packed.exact else torch.float16
     if out is None:
-        out = torch.empty((batch, *grid, cout), device=x.device, dtype=out_dtype)
-    if out.dtype != out_dtype or tuple(out.shape) != (batch, *grid, cout) or out.stride(4) != 1:
+        out_ld = (cout + 7) // 8 * 8
+        out = torch.empty((batch, *grid, out_ld), device=x.device, dtype=out_dtype)[..., :cout]
+    if out.dtype != out_dtype or tuple(out.shape) != (batch, *grid, cout) or (out.stride(4) != 1 and cout != 1):
         raise ValueError(f"out must be {(batch, *grid, cout)} {out_dtype} with unit channel stride")
     res_ld = cout
     if residual is not None:
-        if tuple(residual.shape) != (batch, *grid, cout) or residual.dtype != out_dtype or residual.stride(4) != 1:
-            raise ValueError(f"residual shape {tuple(residual.shape)} {residual.dtype} != output {(batch, *grid, cout)} {out_dtype}")
+        if tuple(residual.shape) != (batch, *grid, cout) or residual.dtype != out_dtype or (
+                residual.stride(4) != 1 and cout != 1):
+            raise ValueError(f"residual shape {tuple(residual.shape)} {residual.dtype} != output "
+                             f"{(batch, *grid, cout)} {out_dtype}")
         res_ld = int(residual.stride(3))
     if bias is not None and (bias.dtype != torch.float32 or bias.numel() != cout or not bias.is_contiguous()):
         raise ValueError("bias must be a contiguous float32 (O,) tensor")
-    if shift is not None and (shift.dtype != torch.float32 or tuple(shift.shape) != (batch, cout) or not shift.is_contiguous()):
+    if shift is not None and (shift.dtype != torch.float32 or tuple(shift.shape) != (batch, cout)
+                              or not shift.is_contiguous()):
         raise ValueError("shift must be a contiguous float32 (B, O) tensor")
+    depth, height, width = (int(s) for s in x.shape[1:4])
     desc = _lib.ConvDesc(
         batch=batch, depth=depth, height=height, width=width, in_channels=cin, x_ld=x_ld,
         out_channels=cout, out_ld=int(out.stride(3)), res_ld=res_ld, mode=mode, exact=int(packed.exact),
@@ -215,8 +236,11 @@ def conv3d_ndhwc(
     if ws_bytes.value:
         workspace = torch.empty(ws_bytes.value, dtype=torch.uint8, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
-    _lib.call(
-        "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
-        _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,
-    )
+    taps = {MODE_POINTWISE: 1, MODE_UP2: 8}.get(mode, 27)
+    flops = 2.0 * batch * grid[0] * grid[1] * grid[2] * cout * taps * cin
+    with instrument.maybe_time("conv3d", flops):
+        _lib.call(
+            "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
+            _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,
+        )
     return out

@@ -96,6 +96,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-collective wait: every lane waits, then the warp reconverges and
+// agrees on the outcome, so the `.sync.aligned` tcgen05 instructions that
+// follow always run with the full warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int* status) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

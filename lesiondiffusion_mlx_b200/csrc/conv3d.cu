@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const TileCoord c = decode_tile(p, t);
       const int acc = local & 1;
-      if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, abort_flag, status)) break;
+      if (!warp_wait(&acc_full[acc], (local >> 1) & 1, abort_flag, status)) break;
       tc_fence_after();
       const long long voxel = row_voxel(p, c, row);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * Cfg::kAccCols;
@@ -468,20 +468,21 @@ int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wm
   // Keep one CTA per SM when the accumulators need more than half of TMEM,
   // so co-resident CTAs never queue on tcgen05.alloc.
   if (Cfg::kTmemCols > 256 && smem < 120 * 1024) smem = 120 * 1024;
-  static bool configured = false;
-  if (!configured) {
-    int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                        "conv smem attribute");
+  static unsigned long long configured = 0;
+  {
+    const int rc = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), 227 * 1024, &configured,
+                                         "conv smem attribute");
     if (rc != LDB_OK) return rc;
-    configured = true;
   }
   kernel<<<grid, kConvThreads, smem, stream>>>(maps, wmap, p, device_status_ptr());
+  count_launch();
   int rc = check_cuda(cudaGetLastError(), "conv3d launch");
   if (rc != LDB_OK) return rc;
   if (p.k_splits > 1) {
     const long long total = static_cast<long long>(p.num_tiles / p.k_splits) * kTileM * (BN / 4);
     const int threads = 256;
     conv_reduce_kernel<BN><<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(p);
+    count_launch();
     rc = check_cuda(cudaGetLastError(), "conv3d split-K reduce launch");
   }
   return rc;

@@ -1,5 +1,6 @@
 #include "host_common.h"
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -9,6 +10,7 @@ __device__ unsigned int g_device_status = 0;
 
 namespace {
 thread_local std::string t_last_error;
+std::atomic<unsigned long long> g_launches{0};
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
@@ -67,6 +69,21 @@ int sm_count() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+void count_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
+
+int ensure_smem_attribute(const void* kernel, int bytes, unsigned long long* flags, const char* what) {
+  static std::mutex mu;
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != LDB_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (*flags & bit) return LDB_OK;
+  rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (rc == LDB_OK) *flags |= bit;
+  return rc;
 }
 
 unsigned int* device_status_ptr() {
@@ -137,5 +154,7 @@ int ldb_device_status(unsigned int* status, int reset) {
 }
 
 int ldb_version(void) { return LDB_ABI_VERSION; }
+
+unsigned long long ldb_launch_count(void) { return ldb::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

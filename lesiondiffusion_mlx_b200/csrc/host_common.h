@@ -29,6 +29,14 @@ int sm_count();
 // Device address of the current device's status word (cached per device).
 unsigned int* device_status_ptr();
 
+// Count one kernel launch issued by the library (see ldb_launch_count).
+void count_launch(int n = 1);
+
+// Raise a kernel's dynamic shared-memory limit once per device (the
+// attribute is per device; setting it again inside a graph capture is
+// avoided).  `flags` is the caller's per-kernel bitset of configured devices.
+int ensure_smem_attribute(const void* kernel, int bytes, unsigned long long* flags, const char* what);
+
 // Encode a tiled tensor map with 16-bit elements.  `dims`/`box` are
 // innermost first; `strides_bytes` has rank-1 entries (dims 1..rank-1).
 // swizzle_bytes is 0, 32, 64 or 128.  Returns LDB_OK or an error code.

@@ -1,0 +1,403 @@
+// GroupNorm statistics, the conv-input "prepare" pass (GN affine + SiLU +
+// f16 rounding or FP32 hi/lo split, with optional two-source channel
+// concatenation) and LayerNorm.  All are HBM-bound: rows are read with
+// 16-byte vector loads, every warp's loads are contiguous, and reductions
+// use warp shuffles plus one shared-memory stage.
+//
+// GroupNorm follows the reference's group_norm_affine / native_group_norm
+// (medmlx-core, used at lesiondiffusion_mlx/mlx_model.py:328-358): biased
+// variance per (batch, group) over the group's channels and all voxels,
+// scale = gamma * rsqrt(var + eps), offset = beta - mean * scale, applied in
+// FP32.  Statistics are accumulated per channel as shifted sums (shift =
+// the channel's value at the first voxel) in FP32 per block and merged in
+// FP64, so large means do not cancel the variance.
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace ldb {
+namespace {
+
+// A virtual NDHWC tensor made of up to two channel blocks [x1 | x2].
+struct Src2 {
+  const void* x1;
+  const void* x2;
+  int c1, c2;      // channels in each block
+  int ld1, ld2;    // channel strides
+  int f32;         // element type: 0 = f16, 1 = f32
+};
+
+__device__ __forceinline__ void load8(const Src2& s, long long voxel, int c, float (&v)[8]) {
+  const void* base;
+  int ld, cc;
+  if (c < s.c1) {
+    base = s.x1;
+    ld = s.ld1;
+    cc = c;
+  } else {
+    base = s.x2;
+    ld = s.ld2;
+    cc = c - s.c1;
+  }
+  if (s.f32) {
+    const float* p = static_cast<const float*>(base) + voxel * ld + cc;
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const __half* p = static_cast<const __half*>(base) + voxel * ld + cc;
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __half22float2(h[q]);
+      v[2 * q] = f.x;
+      v[2 * q + 1] = f.y;
+    }
+  }
+}
+
+// Per-channel shifted partial sums over one chunk of voxels of one batch
+// item.  Block (chunk, b); each thread owns 8 consecutive channels of one
+// voxel row and strides over rows.  partials[b][chunk][c] = (S1, S2).
+__global__ void gn_partial_kernel(Src2 s, int voxels, int chunk_voxels, float2* partials, int nchunks) {
+  const int c_total = s.c1 + s.c2;
+  const int vecs = c_total / 8;
+  const int b = blockIdx.y;
+  const int chunk = blockIdx.x;
+  const int rows_per_iter = blockDim.x / vecs;  // >= 1 by launch configuration
+  const int tid = threadIdx.x;
+  const int lane_vec = tid % vecs;
+  const int row0 = tid / vecs;
+  const bool active = row0 < rows_per_iter;
+  const int c = lane_vec * 8;
+  float shift[8];
+  float s1[8], s2[8];
+  const long long batch_base = static_cast<long long>(b) * voxels;
+  load8(s, batch_base, c, shift);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s1[j] = s2[j] = 0.f;
+  const int v0 = chunk * chunk_voxels;
+  const int v1 = min(voxels, v0 + chunk_voxels);
+  if (active) {
+    for (int v = v0 + row0; v < v1; v += rows_per_iter) {
+      float x[8];
+      load8(s, batch_base + v, c, x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = x[j] - shift[j];
+        s1[j] += d;
+        s2[j] = fmaf(d, d, s2[j]);
+      }
+    }
+  }
+  // Reduce the rows_per_iter threads sharing a channel vector through smem.
+  extern __shared__ float red[];  // [rows_per_iter][c_total][2]
+  if (active) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      red[(row0 * c_total + c + j) * 2] = s1[j];
+      red[(row0 * c_total + c + j) * 2 + 1] = s2[j];
+    }
+  }
+  __syncthreads();
+  for (int ch = tid; ch < c_total; ch += blockDim.x) {
+    float a = 0.f, q = 0.f;
+    for (int r = 0; r < rows_per_iter; ++r) {
+      a += red[(r * c_total + ch) * 2];
+      q += red[(r * c_total + ch) * 2 + 1];
+    }
+    partials[(static_cast<long long>(b) * nchunks + chunk) * c_total + ch] = make_float2(a, q);
+  }
+}
+
+// One block per (batch, group): merge the per-channel partials in FP64 and
+// write the per-channel affine (scale, offset).
+__global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, int nchunks, int groups,
+                                   const float* gamma, const float* beta, float eps, float* affine) {
+  const int c_total = s.c1 + s.c2;
+  const int cpg = c_total / groups;
+  const int b = blockIdx.x / groups;
+  const int g = blockIdx.x % groups;
+  __shared__ double sh_mean[1024];
+  __shared__ double sh_m2[1024];
+  __shared__ double sh_gmean;
+  __shared__ double sh_rstd;
+  const double n = static_cast<double>(voxels);
+  // Channel statistics (one thread per channel of the group).
+  for (int j = threadIdx.x; j < cpg; j += blockDim.x) {
+    const int c = g * cpg + j;
+    double a = 0.0, q = 0.0;
+    for (int k = 0; k < nchunks; ++k) {
+      const float2 p = partials[(static_cast<long long>(b) * nchunks + k) * c_total + c];
+      a += p.x;
+      q += p.y;
+    }
+    // shift of this channel = value at voxel 0
+    const long long v0 = static_cast<long long>(b) * voxels;
+    double shift;
+    if (c < s.c1) {
+      shift = s.f32 ? static_cast<const float*>(s.x1)[v0 * s.ld1 + c]
+                    : __half2float(static_cast<const __half*>(s.x1)[v0 * s.ld1 + c]);
+    } else {
+      const int cc = c - s.c1;
+      shift = s.f32 ? static_cast<const float*>(s.x2)[v0 * s.ld2 + cc]
+                    : __half2float(static_cast<const __half*>(s.x2)[v0 * s.ld2 + cc]);
+    }
+    const double mean_shifted = a / n;
+    sh_mean[j] = shift + mean_shifted;
+    sh_m2[j] = fmax(q - a * mean_shifted, 0.0);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double gm = 0.0;
+    for (int j = 0; j < cpg; ++j) gm += sh_mean[j];
+    gm /= cpg;
+    double m2 = 0.0;
+    for (int j = 0; j < cpg; ++j) {
+      const double d = sh_mean[j] - gm;
+      m2 += sh_m2[j] + n * d * d;
+    }
+    const double var = m2 / (n * cpg);
+    sh_gmean = gm;
+    sh_rstd = 1.0 / sqrt(var + static_cast<double>(eps));
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < cpg; j += blockDim.x) {
+    const int c = g * cpg + j;
+    const float gam = gamma ? gamma[c] : 1.f;
+    const float bet = beta ? beta[c] : 0.f;
+    const float scale = static_cast<float>(static_cast<double>(gam) * sh_rstd);
+    const float offset = static_cast<float>(static_cast<double>(bet) - sh_gmean * static_cast<double>(scale));
+    affine[(static_cast<long long>(b) * c_total + c) * 2] = scale;
+    affine[(static_cast<long long>(b) * c_total + c) * 2 + 1] = offset;
+  }
+}
+
+// out = prepare(x): optional affine (B, C, 2) and SiLU in FP32, then either
+// one f16 rounding or the exact split into hi / 2^11-scaled lo planes
+// (_nax_conv.py:109-155).  Channels past C up to the padded plane width are
+// written as zeros.  One thread per 8 channels of one voxel.
+__global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_batch, const float* affine, int silu,
+                               int split, int cpad, __half* out, int out_ld) {
+  const int c_total = s.c1 + s.c2;
+  const int vecs = cpad / 8;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= voxels_total * vecs) return;
+  const long long voxel = idx / vecs;
+  const int c = static_cast<int>(idx % vecs) * 8;
+  const int b = static_cast<int>(voxel / voxels_per_batch);
+  float v[8];
+  if (c + 8 <= c_total) {
+    load8(s, voxel, c, v);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  }
+  uint4 hi_raw, lo_raw;
+  __half* hi = reinterpret_cast<__half*>(&hi_raw);
+  __half* lo = reinterpret_cast<__half*>(&lo_raw);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float y = 0.f;
+    if (c + j < c_total) {
+      y = v[j];
+      if (affine) {
+        const float* a = affine + (static_cast<long long>(b) * c_total + c + j) * 2;
+        y = fmaf(y, a[0], a[1]);
+      }
+      if (silu) y = silu_f32(y);
+    }
+    hi[j] = __float2half_rn(y);
+    if (split) lo[j] = __float2half_rn((y - __half2float(hi[j])) * 2048.0f);
+  }
+  __half* o = out + voxel * out_ld + c;
+  *reinterpret_cast<uint4*>(o) = hi_raw;
+  if (split) *reinterpret_cast<uint4*>(o + cpad) = lo_raw;
+}
+
+// LayerNorm over the last axis of (rows, C) f16 (mlx_model.py:360-367):
+// FP32 statistics, one rounding.  One warp per row; C <= 1024, C % 8 == 0.
+__global__ void layer_norm_kernel(const __half* x, int x_ld, const float* gamma, const float* beta, float eps,
+                                  __half* out, int out_ld, int rows, int C) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const __half* xr = x + static_cast<long long>(warp) * x_ld;
+  float v[32];
+  int n = 0;
+  float sum = 0.f;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = (it * 32 + lane) * 8;
+    if (c < C) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(h[q]);
+        v[it * 8 + 2 * q] = f.x;
+        v[it * 8 + 2 * q + 1] = f.y;
+        sum += f.x + f.y;
+      }
+      n += 8;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / C;
+  float sq = 0.f;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = (it * 32 + lane) * 8;
+    if (c < C) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[it * 8 + j] - mean;
+        sq = fmaf(d, d, sq);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq / C + eps);
+  __half* orow = out + static_cast<long long>(warp) * out_ld;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = (it * 32 + lane) * 8;
+    if (c < C) {
+      uint4 raw;
+      __half2* h = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = it * 8 + 2 * q;
+        const float a = (v[j] - mean) * rstd * gamma[c + 2 * q] + beta[c + 2 * q];
+        const float b2 = (v[j + 1] - mean) * rstd * gamma[c + 2 * q + 1] + beta[c + 2 * q + 1];
+        h[q] = __floats2half2_rn(a, b2);
+      }
+      *reinterpret_cast<uint4*>(orow + c) = raw;
+    }
+  }
+  (void)n;
+}
+
+int make_src(const void* x1, int c1, int ld1, const void* x2, int c2, int ld2, int dtype, Src2* s) {
+  if (!x1 || c1 <= 0) return fail(LDB_ERR_INVALID, "first source must be non-null with channels > 0");
+  if (c2 > 0 && !x2) return fail(LDB_ERR_INVALID, "second source is null");
+  if (dtype != LDB_F16 && dtype != LDB_F32) return fail(LDB_ERR_INVALID, "dtype must be f16 or f32");
+  if (c1 % 8 || c2 % 8) return fail(LDB_ERR_SHAPE, "channel blocks must be multiples of 8 (got %d, %d)", c1, c2);
+  if (ld1 < c1 || ld1 % 8 || (c2 > 0 && (ld2 < c2 || ld2 % 8)))
+    return fail(LDB_ERR_ALIGNMENT, "channel strides must be >= channels and multiples of 8");
+  s->x1 = x1;
+  s->x2 = c2 > 0 ? x2 : x1;
+  s->c1 = c1;
+  s->c2 = c2 > 0 ? c2 : 0;
+  s->ld1 = ld1;
+  s->ld2 = c2 > 0 ? ld2 : ld1;
+  s->f32 = dtype == LDB_F32;
+  return LDB_OK;
+}
+
+int gn_chunks(int voxels, int batch) {
+  // About 4 blocks per SM overall, at least 32 voxels per block.
+  const int target = std::max(1, (4 * sm_count()) / std::max(1, batch));
+  return std::max(1, std::min(target, (voxels + 31) / 32));
+}
+
+}  // namespace
+}  // namespace ldb
+
+extern "C" {
+
+int ldb_group_norm_workspace_size(int batch, int voxels, int channels, size_t* bytes) {
+  if (!bytes) return ldb::fail(LDB_ERR_INVALID, "bytes is null");
+  if (batch <= 0 || voxels <= 0 || channels <= 0) return ldb::fail(LDB_ERR_SHAPE, "extents must be positive");
+  const int nchunks = ldb::gn_chunks(voxels, batch);
+  *bytes = static_cast<size_t>(batch) * nchunks * channels * sizeof(float2);
+  return LDB_OK;
+}
+
+int ldb_group_norm_affine(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2, int ld2,
+                          int dtype, int batch, int voxels, int groups, const float* gamma, const float* beta,
+                          float eps, float* affine, void* workspace, size_t workspace_bytes) {
+  using namespace ldb;
+  Src2 s;
+  int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
+  if (rc != LDB_OK) return rc;
+  const int C = s.c1 + s.c2;
+  if (batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "batch and voxels must be positive");
+  if (groups <= 0 || C % groups) return fail(LDB_ERR_SHAPE, "groups %d must divide channels %d", groups, C);
+  if (C / groups > 1024) return fail(LDB_ERR_SHAPE, "at most 1024 channels per group");
+  if (C > 8 * 1024) return fail(LDB_ERR_SHAPE, "at most 8192 channels");
+  if (!affine) return fail(LDB_ERR_INVALID, "affine output is null");
+  const int nchunks = gn_chunks(voxels, batch);
+  const size_t need = static_cast<size_t>(batch) * nchunks * C * sizeof(float2);
+  if (!workspace || workspace_bytes < need)
+    return fail(LDB_ERR_WORKSPACE, "group norm needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  const int vecs = C / 8;
+  int threads = 256;
+  if (vecs > threads) threads = ((vecs + 31) / 32) * 32;
+  threads = std::min(threads, 1024);
+  if (vecs > threads) return fail(LDB_ERR_SHAPE, "too many channels for one block row");
+  const int rows = threads / vecs;
+  const size_t smem = static_cast<size_t>(rows) * C * 2 * sizeof(float);
+  if (smem > 200 * 1024) return fail(LDB_ERR_SHAPE, "group norm reduction exceeds shared memory");
+  if (smem > 48 * 1024) {
+    static unsigned long long configured = 0;
+    rc = ensure_smem_attribute(reinterpret_cast<const void*>(gn_partial_kernel), 200 * 1024, &configured,
+                               "gn smem attribute");
+    if (rc != LDB_OK) return rc;
+  }
+  const int chunk_voxels = (voxels + nchunks - 1) / nchunks;
+  float2* partials = static_cast<float2*>(workspace);
+  gn_partial_kernel<<<dim3(nchunks, batch), threads, smem, stream>>>(s, voxels, chunk_voxels, partials, nchunks);
+  count_launch();
+  rc = check_cuda(cudaGetLastError(), "gn_partial launch");
+  if (rc != LDB_OK) return rc;
+  gn_finalize_kernel<<<batch * groups, 128, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
+                                                         affine);
+  count_launch();
+  return check_cuda(cudaGetLastError(), "gn_finalize launch");
+}
+
+int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2, int ld2,
+                      int dtype, int batch, int voxels, const float* affine, int silu, int split, void* out,
+                      int out_ld) {
+  using namespace ldb;
+  Src2 s;
+  int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
+  if (rc != LDB_OK) return rc;
+  if (!out) return fail(LDB_ERR_INVALID, "out is null");
+  const int C = s.c1 + s.c2;
+  const int cpad = split ? ((C + 15) / 16) * 16 : ((C + 7) / 8) * 8;
+  if (out_ld % 8 || out_ld < (split ? 2 * cpad : cpad))
+    return fail(LDB_ERR_ALIGNMENT, "out_ld %d too small or not a multiple of 8", out_ld);
+  const long long total = static_cast<long long>(batch) * voxels * (cpad / 8);
+  if (total <= 0) return fail(LDB_ERR_SHAPE, "empty input");
+  const int threads = 256;
+  prepare_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
+      s, static_cast<long long>(batch) * voxels, voxels, affine, silu, split, cpad, static_cast<__half*>(out),
+      out_ld);
+  count_launch();
+  return check_cuda(cudaGetLastError(), "prepare launch");
+}
+
+int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,
+                   void* out, int out_ld, int rows, int channels) {
+  using namespace ldb;
+  if (!x || !out || !gamma || !beta) return fail(LDB_ERR_INVALID, "layer_norm: null pointer");
+  if (channels <= 0 || channels > 1024 || channels % 8) return fail(LDB_ERR_SHAPE, "channels must be 8..1024, %% 8");
+  if (x_ld % 8 || out_ld % 8) return fail(LDB_ERR_ALIGNMENT, "row strides must be multiples of 8");
+  if (rows <= 0) return fail(LDB_ERR_SHAPE, "rows must be positive");
+  const int threads = 256;
+  const long long blocks = (static_cast<long long>(rows) * 32 + threads - 1) / threads;
+  layer_norm_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      static_cast<const __half*>(x), x_ld, gamma, beta, eps, static_cast<__half*>(out), out_ld, rows, channels);
+  count_launch();
+  return check_cuda(cudaGetLastError(), "layer_norm launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,360 @@
+"""B200 networks of the hot path: the 3-D LDM UNet denoiser and the VQ
+decoder, composed from the sm_100a operators.
+
+These mirror ``LdmUnet`` and ``VqAutoencoder`` of lesiondiffusion_mlx
+(mlx_model.py:384-819) on the native (conditioned-mode) arithmetic, but keep
+every activation NDHWC on the device:
+
+* ``norm_silu_conv`` = GroupNorm statistics -> one prepare pass (affine +
+  SiLU, f16 rounding; also fuses the skip concatenation) -> tcgen05 conv
+  with bias, per-batch shift and residual in its epilogue.
+* Transformer tokens are the NDHWC voxels themselves (no transposes); Q, K
+  and V come from one fused projection GEMM; residual adds and GELU live in
+  the GEMM epilogues; attention is the tcgen05 flash kernel.
+* The time-embedding MLP and every residual block's embedding projection
+  are skinny GEMMs (rows = batch).
+
+Weights use the reference's state-dict names and are packed once at
+construction.  Forward passes allocate through PyTorch's caching allocator,
+so a whole step can be captured in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import re
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops
+from .conv import PackedWeight, conv3d_ndhwc, pack_upsample_weight, pack_weight
+
+UPSAMPLE_CONV = re.compile(r"(?:^output_blocks\.\d+\.\d+|\.upsample)\.conv$")
+
+
+@dataclass(frozen=True)
+class UnetConfig:
+    """UNet architecture (mlx_model.py:45-72)."""
+
+    model_channels: int
+    num_res_blocks: int
+    attention_resolutions: tuple[int, ...]
+    channel_mult: tuple[int, ...] = (1, 2, 4)
+    num_head_channels: int = 32
+    skip_context: bool = False
+
+
+class _Params:
+    """Device copies of a reference-named state dict, packed on first use."""
+
+    def __init__(self, weights: dict[str, torch.Tensor], device: torch.device, dtype: torch.dtype):
+        self.raw = weights
+        self.device = device
+        self.dtype = dtype
+        self._cache: dict[tuple[str, str], object] = {}
+
+    def has(self, name: str) -> bool:
+        return name in self.raw
+
+    def _get(self, kind: str, key: str, build):
+        k = (kind, key)
+        if k not in self._cache:
+            self._cache[k] = build()
+        return self._cache[k]
+
+    def f32(self, name: str) -> torch.Tensor | None:
+        if name not in self.raw:
+            return None
+        return self._get("f32", name, lambda: self.raw[name].to(self.device, torch.float32).contiguous())
+
+    def f16(self, name: str) -> torch.Tensor:
+        return self._get("f16", name, lambda: self.raw[name].to(self.device, torch.float16).contiguous())
+
+    def conv(self, key: str, stride: int = 1) -> PackedWeight:
+        def build():
+            w = self.raw[key + ".weight"].to(self.device, self.dtype)
+            if UPSAMPLE_CONV.search(key):
+                return pack_upsample_weight(w)
+            return pack_weight(w, stride=stride)
+
+        return self._get(f"conv{stride}", key, build)
+
+    def dense_packed(self, *keys: str) -> PackedWeight:
+        """Pointwise-packed dense weight; several keys are stacked along outputs (fused Q/K/V)."""
+
+        def build():
+            ws = [self.raw[k + ".weight"] for k in keys]
+            w = torch.cat([t.reshape(t.shape[0], -1) for t in ws], 0).to(self.device, self.dtype)
+            return pack_weight(w[:, :, None, None, None])
+
+        return self._get("dense", "|".join(keys), build)
+
+    def dense_bias(self, *keys: str) -> torch.Tensor | None:
+        def build():
+            parts = []
+            for k in keys:
+                b = self.raw.get(k + ".bias")
+                if b is None:
+                    n = self.raw[k + ".weight"].shape[0]
+                    b = torch.zeros(n, dtype=self.dtype)
+                parts.append(b.to(self.dtype))
+            if all(self.raw.get(k + ".bias") is None for k in keys):
+                return None
+            return torch.cat(parts).to(self.device, torch.float32).contiguous()
+
+        return self._get("dbias", "|".join(keys), build)
+
+
+def _voxels(x: torch.Tensor) -> tuple[int, int, int]:
+    return int(x.shape[1]), int(x.shape[2]), int(x.shape[3])
+
+
+class _Layers:
+    def __init__(self, params: _Params):
+        self.p = params
+
+    def conv(self, x: torch.Tensor, key: str, *, stride: int = 1, residual: torch.Tensor | None = None,
+             shift: torch.Tensor | None = None, output_scale: float = 1.0) -> torch.Tensor:
+        """3x3x3 (stride 1/2, or folded up-2x) or pointwise conv of NDHWC f16 x."""
+        packed = self.p.conv(key, stride)
+        return conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
+                            output_scale=output_scale)
+
+    def norm_silu_conv(self, x: torch.Tensor, norm_key: str, conv_key: str, *, groups: int, eps: float,
+                       shift: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                       x2: torch.Tensor | None = None, output_scale: float = 1.0) -> torch.Tensor:
+        """``residual + conv(SiLU(GN([x | x2]))) + shift`` (mlx_model.py:290-342)."""
+        affine = ops.group_norm_affine(x, self.p.f32(norm_key + ".weight"), self.p.f32(norm_key + ".bias"),
+                                       groups=groups, eps=eps, x2=x2)
+        prepared = ops.prepare_input(x, affine=affine, silu=True, x2=x2)
+        return self.conv(prepared, conv_key, residual=residual, shift=shift, output_scale=output_scale)
+
+    def dense(self, x: torch.Tensor, *keys: str, residual: torch.Tensor | None = None,
+              act: int = _lib.LDB_ACT_NONE) -> torch.Tensor:
+        """Linear layer(s) on token rows (B, L, C) via the pointwise tensor-core conv."""
+        packed = self.p.dense_packed(*keys)
+        bias = self.p.dense_bias(*keys)
+        b, length, c = (int(s) for s in x.shape)
+        x5 = x.unsqueeze(1).unsqueeze(1)
+        res5 = None if residual is None else residual.unsqueeze(1).unsqueeze(1)
+        out = conv3d_ndhwc(x5, packed, bias, residual=res5, act=act)
+        return out.view(b, length, packed.out_channels)
+
+
+class LdmUnetB200(_Layers):
+    """The LDM UNet (mlx_model.py:384-654) on B200 kernels, NDHWC f16."""
+
+    def __init__(self, weights: dict[str, torch.Tensor], config: UnetConfig, *, device: torch.device | str = "cuda",
+                 dtype: torch.dtype = torch.float16):
+        if dtype != torch.float16:
+            raise ValueError("the B200 UNet runs in float16 (the LINet checkpoint dtype)")
+        super().__init__(_Params(weights, torch.device(device), dtype))
+        self.config = config
+        self.device = torch.device(device)
+        self.in_channels = int(weights["input_blocks.0.0.weight"].shape[1])
+        self.out_channels = int(weights["out.2.weight"].shape[0])
+        self._pack_all()
+
+    def _pack_all(self) -> None:
+        """Pack every weight now so a captured step holds no packing work."""
+        for name in self.p.raw:
+            if not name.endswith(".weight"):
+                continue
+            key = name[: -len(".weight")]
+            w = self.p.raw[name]
+            if w.ndim == 5 and w.shape[2:] == (3, 3, 3):
+                self.p.conv(key, 2 if key.endswith(".op") else 1)
+            elif w.ndim == 5:
+                self.p.conv(key)
+            self.p.f32(key + ".bias")
+        for name in self.p.raw:
+            if name.endswith(".norm.weight") or re.search(r"(in_layers\.0|out_layers\.0|norm[123]|out\.0)\.weight$", name):
+                self.p.f32(name)
+                self.p.f32(name[: -len("weight")] + "bias")
+
+    # ------------------------------------------------------------- blocks
+
+    def time_embedding(self, timesteps: torch.Tensor, step: torch.Tensor | None = None) -> torch.Tensor:
+        """mlx_model.py:609-614; ``timesteps`` int32 (B,) or a (steps, B) table read at ``*step``."""
+        emb = ops.timestep_embedding(timesteps, self.config.model_channels, step=step, out_dtype=torch.float16)
+        h = ops.dense_small(emb, self.p.f16("time_embed.0.weight"), self.p.f32("time_embed.0.bias"))
+        return ops.dense_small(h, self.p.f16("time_embed.2.weight"), self.p.f32("time_embed.2.bias"), in_silu=True)
+
+    def residual(self, x: torch.Tensor, emb: torch.Tensor, key: str, x2: torch.Tensor | None = None) -> torch.Tensor:
+        """mlx_model.py:420-441 (with the skip concatenation [x | x2] fused into the norm pass)."""
+        channels = int(x.shape[-1]) + (0 if x2 is None else int(x2.shape[-1]))
+        groups = 32 if channels % 32 == 0 else channels
+        shift = ops.dense_small(emb, self.p.f16(key + ".emb_layers.1.weight"), self.p.f32(key + ".emb_layers.1.bias"),
+                                in_silu=True, out_dtype=torch.float32, round_f16=True)
+        h = self.norm_silu_conv(x, key + ".in_layers.0", key + ".in_layers.2", groups=groups, eps=1e-5,
+                                shift=shift, x2=x2)
+        out_c = int(h.shape[-1])
+        groups = 32 if out_c % 32 == 0 else out_c
+        if self.p.has(key + ".skip_connection.weight"):
+            cat = x if x2 is None else ops.prepare_input(x, x2=x2)
+            skip = self.conv(cat, key + ".skip_connection")
+        else:
+            skip = x
+        return self.norm_silu_conv(h, key + ".out_layers.0", key + ".out_layers.3", groups=groups, eps=1e-5,
+                                   residual=skip)
+
+    def attention(self, x: torch.Tensor, key: str, heads: int, kv: tuple[torch.Tensor, torch.Tensor] | None,
+                  residual: torch.Tensor) -> torch.Tensor:
+        """``residual + to_out(attention(x, context))`` (mlx_model.py:443-493)."""
+        c = int(x.shape[-1])
+        if kv is None:
+            qkv = self.dense(x, key + ".to_q", key + ".to_k", key + ".to_v")
+            q, k, v = qkv[..., :c], qkv[..., c : 2 * c], qkv[..., 2 * c :]
+        else:
+            q = self.dense(x, key + ".to_q")
+            k, v = kv
+        depth = c // heads
+        attn = ops.flash_attention(q, k, v, heads=heads, scale=depth ** -0.5)
+        return self.dense(attn, key + ".to_out.0", residual=residual)
+
+    def transformer(self, x: torch.Tensor, key: str, cache: dict) -> torch.Tensor:
+        """mlx_model.py:522-552 on NDHWC tokens."""
+        b = int(x.shape[0])
+        c = int(x.shape[-1])
+        affine = ops.group_norm_affine(x, self.p.f32(key + ".norm.weight"), self.p.f32(key + ".norm.bias"),
+                                       groups=32, eps=1e-6)
+        normed = ops.prepare_input(x, affine=affine)
+        t = self.conv(normed, key + ".proj_in")
+        tokens = t.view(b, -1, c)
+        heads = c // self.config.num_head_channels
+        blk = key + ".transformer_blocks.0"
+
+        def ln(t_: torch.Tensor, n: str) -> torch.Tensor:
+            return ops.layer_norm(t_, self.p.f32(f"{blk}.{n}.weight"), self.p.f32(f"{blk}.{n}.bias"), 1e-5)
+
+        tokens = self.attention(ln(tokens, "norm1"), blk + ".attn1", heads, None, tokens)
+        tokens = self.attention(ln(tokens, "norm2"), blk + ".attn2", heads, cache.get(blk + ".attn2"), tokens)
+        ff = self.dense(ln(tokens, "norm3"), blk + ".ff.net.0.0", act=_lib.LDB_ACT_GELU)
+        tokens = self.dense(ff, blk + ".ff.net.2", residual=tokens)
+        return self.conv(tokens.view(t.shape), key + ".proj_out", residual=x)
+
+    def prepare_context(self, context: torch.Tensor | None) -> dict:
+        """Project the context and every attn2 K/V once per binding (mlx_model.py:570-597)."""
+        if context is None or self.config.skip_context:
+            return {}
+        ctx = context.to(self.device, torch.float16).contiguous()
+        if ctx.shape[-1] % 8:
+            ctx = torch.nn.functional.pad(ctx, (0, 8 - ctx.shape[-1] % 8))[..., : context.shape[-1]]
+        projected = self.dense(ctx, "context_linear_projection")
+        cache = {}
+        for name in self.p.raw:
+            if name.endswith(".attn2.to_k.weight"):
+                key = name[: -len(".to_k.weight")]
+                c = int(self.p.raw[key + ".to_k.weight"].shape[0])
+                kv = self.dense(projected, key + ".to_k", key + ".to_v")
+                cache[key] = (kv[..., :c], kv[..., c:])
+        return cache
+
+    def forward(self, x: torch.Tensor, timesteps: torch.Tensor, cache: dict, step: torch.Tensor | None = None
+                ) -> torch.Tensor:
+        """Noise prediction for NDHWC f16 ``x`` (B, D, H, W, C_in) (mlx_model.py:599-654)."""
+        cfg = self.config
+        emb = self.time_embedding(timesteps, step)
+        h = self.conv(x, "input_blocks.0.0")
+        skips = [h]
+        block, resolution = 1, 1
+        for level in range(len(cfg.channel_mult)):
+            for _ in range(cfg.num_res_blocks):
+                key = f"input_blocks.{block}"
+                h = self.residual(h, emb, key + ".0")
+                if resolution in cfg.attention_resolutions:
+                    h = self.transformer(h, key + ".1", cache)
+                skips.append(h)
+                block += 1
+            if level < len(cfg.channel_mult) - 1:
+                h = self.conv(h, f"input_blocks.{block}.0.op", stride=2)
+                skips.append(h)
+                block += 1
+                resolution *= 2
+        h = self.residual(h, emb, "middle_block.0")
+        h = self.transformer(h, "middle_block.1", cache)
+        h = self.residual(h, emb, "middle_block.2")
+        block = 0
+        for level in reversed(range(len(cfg.channel_mult))):
+            for i in range(cfg.num_res_blocks + 1):
+                key = f"output_blocks.{block}"
+                h = self.residual(h, emb, key + ".0", x2=skips.pop())
+                has_attention = resolution in cfg.attention_resolutions
+                if has_attention:
+                    h = self.transformer(h, key + ".1", cache)
+                if level and i == cfg.num_res_blocks:
+                    h = self.conv(h, key + f".{2 if has_attention else 1}.conv")
+                    resolution //= 2
+                block += 1
+        groups = 32 if h.shape[-1] % 32 == 0 else int(h.shape[-1])
+        return self.norm_silu_conv(h, "out.0", "out.2", groups=groups, eps=1e-5)
+
+    def __call__(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor | None) -> torch.Tensor:
+        return self.forward(x, timesteps, self.prepare_context(context))
+
+
+class VqDecoderB200(_Layers):
+    """VQ quantize + decode (mlx_model.py:742-819) on B200 kernels, NDHWC.
+
+    ``levels`` lists decoder levels from the top (first run) down with
+    ``(blocks, upsample_after)``; the reference's LINet VQ is 3 levels with
+    one upsample after level 1 (the default).  ``scaled`` selects the
+    scaled-f16 decode of ScaledVqDecoder (_scaled_vq.py:27-118).
+    """
+
+    SCALE = 0.25
+
+    def __init__(self, weights: dict[str, torch.Tensor], *, device: torch.device | str = "cuda",
+                 dtype: torch.dtype = torch.float16, groups: int = 16, scaled: bool = False):
+        if dtype != torch.float16:
+            raise ValueError("the B200 decoder runs in float16")
+        super().__init__(_Params(weights, torch.device(device), dtype))
+        self.device = torch.device(device)
+        self.groups = groups
+        self.scaled = scaled
+        names = set(weights)
+        self.levels = sorted({int(m.group(1)) for n in names if (m := re.match(r"decoder\.up\.(\d+)\.", n))},
+                             reverse=True)
+        self.blocks = {lvl: sorted({int(m.group(1)) for n in names
+                                    if (m := re.match(rf"decoder\.up\.{lvl}\.block\.(\d+)\.", n))})
+                       for lvl in self.levels}
+        self.codebook = weights["quantize.embedding.weight"].to(self.device, torch.float16).contiguous()
+        for name in names:
+            if name.endswith(".weight") and weights[name].ndim == 5:
+                self.p.conv(name[: -len(".weight")])
+
+    def residual(self, x: torch.Tensor, key: str, scaled_in: bool = False, scaled_out: bool = False) -> torch.Tensor:
+        """mlx_model.py:720-727 (+ _scaled_vq.py:75-118 scaling)."""
+        eps1 = 1e-6 * (self.SCALE ** 2 if scaled_in else 1.0)
+        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=self.groups, eps=eps1)
+        skip = self.conv(x, key + ".nin_shortcut") if self.p.has(key + ".nin_shortcut.weight") else x
+        return self.norm_silu_conv(h, key + ".norm2", key + ".conv2", groups=self.groups, eps=1e-6, residual=skip,
+                                   output_scale=self.SCALE if scaled_out else 1.0)
+
+    def quantize(self, z: torch.Tensor) -> torch.Tensor:
+        """Nearest code + straight-through value (mlx_model.py:742-803)."""
+        c = int(z.shape[-1])
+        buf = torch.zeros((*z.shape[:-1], (c + 7) // 8 * 8), dtype=z.dtype, device=z.device)
+        q = buf[..., :c]
+        ops.vq_nearest4(z, self.codebook, quantized=q)
+        return q
+
+    def decode(self, z: torch.Tensor, *, quantize: bool = True, to_hu: bool = False) -> torch.Tensor:
+        """Decode NDHWC f16 latent ``z`` (B, d, h, w, C) to (B, 2d, 2h, 2w, C_out) (mlx_model.py:805-819)."""
+        x = self.quantize(z) if quantize else z
+        x = self.conv(x, "post_quant_conv")
+        x = self.conv(x, "decoder.conv_in")
+        x = self.residual(x, "decoder.mid.block_1")
+        x = self.residual(x, "decoder.mid.block_2")
+        upsampled = False
+        for level in self.levels:
+            for block in self.blocks[level]:
+                key = f"decoder.up.{level}.block.{block}"
+                x = self.residual(x, key, scaled_in=self.scaled and upsampled, scaled_out=self.scaled and upsampled)
+            if self.p.has(f"decoder.up.{level}.upsample.conv.weight"):
+                x = self.conv(x, f"decoder.up.{level}.upsample.conv",
+                              output_scale=self.SCALE if self.scaled else 1.0)
+                upsampled = True
+        eps = 1e-6 * (self.SCALE ** 2 if self.scaled else 1.0)
+        out = self.norm_silu_conv(x, "decoder.norm_out", "decoder.conv_out", groups=self.groups, eps=eps)
+        return ops.hu_map(out) if to_hu else out

@@ -34,10 +34,31 @@ class UnetConfig:
     skip_context: bool = False
 
 
+class _ComputeCache(dict):
+    """The weight dict, plus cached compute-dtype copies of every tensor.
+
+    Lookups return the stored tensors unchanged; ``ops`` converts operands
+    with ``.to(compute)``, which is free for tensors already in that dtype, so
+    conversions are done once here instead of on every call.
+    """
+
+    def __init__(self, weights: dict[str, torch.Tensor], compute: torch.dtype):
+        super().__init__(weights)
+        self.compute = compute
+        self.converted: dict[str, torch.Tensor] = {}
+
+    def as_compute(self, key: str) -> torch.Tensor:
+        t = self.converted.get(key)
+        if t is None:
+            t = self[key].to(self.compute)
+            self.converted[key] = t
+        return t
+
+
 class OracleLayers:
     def __init__(self, weights: dict[str, torch.Tensor], *, source_rounding: bool = False,
                  compute: torch.dtype = ops.DEFAULT_COMPUTE):
-        self.w = weights
+        self.w = _ComputeCache(weights, compute)
         self.source_rounding = source_rounding
         self.compute = compute
 
@@ -46,14 +67,15 @@ class OracleLayers:
 
     def conv(self, x: torch.Tensor, key: str, *, padding: int = 1, stride: int = 1) -> torch.Tensor:
         """mlx_model.py:159-202: 3x3x3 rounds once; 1x1x1 rounds the product then the bias add."""
-        weight = self.w[key + ".weight"]
+        weight = self.w.as_compute(key + ".weight")
         if weight.shape[2:] == (1, 1, 1) and padding == 0:
             return ops.pointwise_conv(x, weight, self._bias(key), dtype=x.dtype, compute=self.compute)
         return ops.conv3d(x, weight, self._bias(key), stride=stride, padding=padding, dtype=x.dtype,
                           compute=self.compute)
 
     def dense(self, x: torch.Tensor, key: str) -> torch.Tensor:
-        return ops.dense(x, self.w[key + ".weight"], self._bias(key), dtype=x.dtype, compute=self.compute)
+        return ops.dense(x, self.w.as_compute(key + ".weight"), self._bias(key), dtype=x.dtype,
+                         compute=self.compute)
 
     def norm(self, x: torch.Tensor, key: str, *, groups: int, eps: float, silu: bool = False) -> torch.Tensor:
         return ops.native_group_norm(x, self.w[key + ".weight"], self.w[key + ".bias"], groups=groups, eps=eps,
@@ -71,7 +93,7 @@ class OracleLayers:
                 y = (residual.to(torch.float32) + y.to(torch.float32)).to(x.dtype)
             return y
         return ops.norm_silu_conv(
-            x, self.w[norm_key + ".weight"], self.w[norm_key + ".bias"], self.w[conv_key + ".weight"],
+            x, self.w[norm_key + ".weight"], self.w[norm_key + ".bias"], self.w.as_compute(conv_key + ".weight"),
             self._bias(conv_key), groups=groups, eps=eps, shift=shift, residual=residual,
             output_scale=output_scale, compute=self.compute,
         )

@@ -238,7 +238,8 @@ def upsample_nearest2(x: torch.Tensor) -> torch.Tensor:
 def resize_nearest(x: torch.Tensor, shape: tuple[int, int, int]) -> torch.Tensor:
     """Resize with source index ``floor(i * in / out)`` per axis (_spatial.py:60-69)."""
     for axis, target in enumerate(shape, start=2):
-        idx = torch.floor(torch.arange(target, dtype=torch.float64) * (x.shape[axis] / target)).to(torch.int64)
+        ratio = torch.tensor(x.shape[axis] / target, dtype=torch.float32)
+        idx = torch.floor(torch.arange(target, dtype=torch.float32) * ratio).to(torch.int64)
         x = x.index_select(axis, idx)
     return x
 

@@ -1,0 +1,126 @@
+"""Host-side logic that needs no GPU: the C library loads and exports every
+declared symbol, conv planning (geometry, workspace, packed-weight rows),
+sampler schedules and coefficients vs the oracle, and weight packing."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for header in (ROOT / "include").glob("*.h"):
+        names += re.findall(r"^LDB_API [^(]*?\b(ldb_\w+)\s*\(", header.read_text(), flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from lesiondiffusion_mlx_b200 import _lib
+
+    lib = _lib.library()
+    names = declared_symbols()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.ldb_version() == 1
+
+
+def test_errors_are_reported_without_a_device():
+    from lesiondiffusion_mlx_b200 import _lib
+
+    desc = _lib.ConvDesc(batch=1, depth=2, height=2, width=2, in_channels=16, x_ld=20, out_channels=8, out_ld=8,
+                         res_ld=8, mode=0, exact=0, out_dtype=0, act=0, output_scale=1.0)
+    size = ctypes.c_size_t(0)
+    with pytest.raises(_lib.LdbError, match="multiple of 8"):
+        _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(size))
+    desc.x_ld = 16
+    desc.mode = 9
+    with pytest.raises(_lib.LdbError, match="unknown conv mode"):
+        _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(size))
+
+
+@pytest.mark.parametrize("cin,cout,exact,rows,k", [(128, 128, False, 128, 27 * 128), (8, 8, False, 16, 27 * 16),
+                                                    (512, 384, False, 512, 27 * 512), (4, 16, True, 16, 2 * 27 * 16),
+                                                    (256, 40, False, 64, 27 * 256)])
+def test_conv_weight_geometry(cin, cout, exact, rows, k):
+    from lesiondiffusion_mlx_b200 import _lib
+
+    desc = _lib.ConvDesc(batch=1, depth=1, height=1, width=1, in_channels=cin,
+                         x_ld=max(8, 2 * ((cin + 15) // 16) * 16 if exact else (cin + 7) // 8 * 8),
+                         out_channels=cout, out_ld=cout, res_ld=cout, mode=0, exact=int(exact), out_dtype=0, act=0,
+                         output_scale=1.0)
+    r, kt = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.call("ldb_conv3d_weight_rows", ctypes.byref(desc), ctypes.byref(r), ctypes.byref(kt))
+    assert (r.value, kt.value) == (rows, k)
+
+
+def test_split_k_workspace_only_for_small_grids():
+    from lesiondiffusion_mlx_b200 import _lib
+
+    def ws(d, h, w, cin):
+        desc = _lib.ConvDesc(batch=1, depth=d, height=h, width=w, in_channels=cin, x_ld=cin, out_channels=512,
+                             out_ld=512, res_ld=512, mode=0, exact=0, out_dtype=0, act=0, output_scale=1.0)
+        size = ctypes.c_size_t(0)
+        _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(size))
+        return size.value
+
+    assert ws(8, 10, 10, 512) > 0  # 800 voxels: too few tiles, K is split
+    assert ws(32, 40, 40, 128) == 0  # 400 brick tiles fill the GPU
+
+
+def test_conv_geometry_uses_input_extents():
+    from lesiondiffusion_mlx_b200.conv import MODE_CONV, MODE_STRIDE2, MODE_UP2, PackedWeight, conv_geometry
+
+    x = torch.empty((2, 5, 7, 9, 24))[..., :20]
+    conv = PackedWeight(torch.empty(0), "conv", 20, 40, False)
+    assert conv_geometry(tuple(x.shape), tuple(x.stride()), conv) == (MODE_CONV, (5, 7, 9), 24, 20)
+    assert conv_geometry(tuple(x.shape), tuple(x.stride()), conv, stride=2) == (MODE_STRIDE2, (3, 4, 5), 24, 20)
+    up = PackedWeight(torch.empty(0), "up", 20, 40, False)
+    assert conv_geometry(tuple(x.shape), tuple(x.stride()), up) == (MODE_UP2, (10, 14, 18), 24, 20)
+    with pytest.raises(ValueError, match="dense over voxels"):
+        y = torch.empty((2, 5, 7, 10, 24))[:, :, :, :9, :20]
+        conv_geometry(tuple(y.shape), tuple(y.stride()), conv)
+
+
+def test_upsample_fold_matches_conv_of_upsampled_input():
+    """The packed parity fold reproduces conv(upsample2(x)) (checked on CPU in float64)."""
+    from lesiondiffusion_mlx_b200.conv import pack_upsample_weight
+    from oracle import ops as oops
+
+    rng = np.random.default_rng(4)
+    w = torch.from_numpy(rng.normal(size=(8, 16, 3, 3, 3)).astype(np.float32))
+    x = torch.from_numpy(rng.normal(size=(1, 16, 3, 4, 5)))
+    ref = torch.nn.functional.conv3d(oops.upsample_nearest2(x), w.double(), padding=1)
+    got = oops.upsample_conv(x, w, None, dtype=torch.float64, compute=torch.float64)
+    assert torch.allclose(got, ref, atol=1e-5)
+    packed = pack_upsample_weight(w)
+    assert packed.exact and packed.kind == "up" and packed.tensor.shape == (8 * 16, 2 * 8 * 16)
+
+
+def test_sampler_tables_match_oracle():
+    from lesiondiffusion_mlx_b200.sampling import DdimSampler, Dpmpp2mSampler
+    from oracle import samplers as osamp
+
+    with np.load(ROOT / "tests/golden/reference_fixtures.npz") as g:
+        acp = g["dpmpp_2m/linet_25.alphas_cumprod"]
+    d = DdimSampler(acp, 200)
+    ref = osamp.ddim_coefficients(acp, 200)
+    assert d.timesteps == tuple(ref["timesteps"])
+    np.testing.assert_array_equal(d.sigmas, ref["sigmas"])
+    np.testing.assert_array_equal(d.coefficients[0, :4], [ref["alphas"][-1], ref["previous"][-1],
+                                                           ref["sigmas"][-1], ref["sqrt_one_minus"][-1]])
+    p = Dpmpp2mSampler(acp, 50)
+    ts, coeffs = osamp.dpm_coefficients(acp, 50)
+    assert p.timesteps == ts
+    np.testing.assert_array_equal(p.coefficients, coeffs)
+    with pytest.raises(ValueError):
+        DdimSampler(acp, 3)
