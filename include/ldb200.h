@@ -128,6 +128,21 @@ LDB_API int ldb_group_norm_affine(ldb_stream_t stream, const void* x1, int c1, i
                                   const float* beta, float eps, float* affine, void* workspace,
                                   size_t workspace_bytes);
 
+/* Allocation-free variant of ldb_group_norm_affine (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they
+ * call -- e.g. an engine that owns every device allocation up front, or a
+ * binding without access to a device allocator -- so they cannot provide a
+ * workspace.  The partial sums use a fixed 4 MiB device array inside the
+ * library (held by every GPU that loads it until exit), so
+ * batch * channels must not exceed 524288; larger calls fail with
+ * LDB_ERR_SHAPE.  Performs no cudaMalloc / cudaFree.  The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race.
+ * Same arguments and results as ldb_group_norm_affine without the workspace. */
+LDB_API int ldb_group_norm_affine_noalloc(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2,
+                                          int c2, int ld2, int dtype, int batch, int voxels, int groups,
+                                          const float* gamma, const float* beta, float eps, float* affine);
+
 /* Conv-input preparation: replaces the pack kernel of _nax_conv.py:109-155
  * (and native_group_norm, mlx_model.py:348-358, when used with an affine).
  * out = f16(silu?(x * scale + offset)) over [x1 | x2], or with split = 1 the

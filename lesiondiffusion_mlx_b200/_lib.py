@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_conv3d_fwd": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _SZ],
     "ldb_group_norm_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
     "ldb_group_norm_affine": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _SZ],
+    "ldb_group_norm_affine_noalloc": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P],
     "ldb_prepare_input": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I],
     "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
     "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],

@@ -13,6 +13,8 @@
 // FP64, so large means do not cancel the variance.
 
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -308,6 +310,39 @@ int gn_chunks(int voxels, int batch) {
 }
 
 }  // namespace
+
+// Fixed scratch for ldb_group_norm_affine_noalloc: the per-(batch, chunk,
+// channel) partial sums live in this file-scope device array instead of a
+// caller workspace.  4 MiB (524288 float2 entries); every GPU that loads the
+// library holds it until the process exits.
+constexpr long long kNoAllocGnEntries = 1LL << 19;
+static __device__ __align__(256) float2 g_gn_noalloc_scratch[kNoAllocGnEntries];
+
+namespace {
+
+// Device address of the scratch array for the current device.  Host code
+// cannot use the symbol itself (on the host it names a stand-in, not device
+// memory), so the address is looked up once per device with that device
+// current and cached.
+int noalloc_scratch(float2** out) {
+  static std::mutex mu;
+  static std::vector<float2*> cache;
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != LDB_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_gn_noalloc_scratch), "cudaGetSymbolAddress(group-norm scratch)");
+    if (rc != LDB_OK) return rc;
+    cache[dev] = static_cast<float2*>(p);
+  }
+  *out = cache[dev];
+  return LDB_OK;
+}
+
+}  // namespace
 }  // namespace ldb
 
 extern "C" {
@@ -398,6 +433,61 @@ int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* ga
       static_cast<const __half*>(x), x_ld, gamma, beta, eps, static_cast<__half*>(out), out_ld, rows, channels);
   count_launch();
   return check_cuda(cudaGetLastError(), "layer_norm launch");
+}
+
+// GroupNorm affine without any allocation: the same statistics as
+// ldb_group_norm_affine, with the partial sums kept in the library's fixed
+// device scratch (g_gn_noalloc_scratch) instead of a caller workspace.  For
+// callers that cannot allocate device memory at call time.  The first call
+// on a device looks up the scratch address (make it before any stream
+// capture).  Calls share the scratch, so calls that overlap on the GPU
+// (different streams, or different host threads) race; each call fully
+// writes every partial it reads, so nothing needs clearing between calls.
+int ldb_group_norm_affine_noalloc(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
+                                  int ld2, int dtype, int batch, int voxels, int groups, const float* gamma,
+                                  const float* beta, float eps, float* affine) {
+  using namespace ldb;
+  Src2 s;
+  int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
+  if (rc != LDB_OK) return rc;
+  const int C = s.c1 + s.c2;
+  if (batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "batch and voxels must be positive");
+  if (groups <= 0 || C % groups) return fail(LDB_ERR_SHAPE, "groups %d must divide channels %d", groups, C);
+  if (C / groups > 1024) return fail(LDB_ERR_SHAPE, "at most 1024 channels per group");
+  if (C > 8 * 1024) return fail(LDB_ERR_SHAPE, "at most 8192 channels");
+  if (!affine) return fail(LDB_ERR_INVALID, "affine output is null");
+  const long long per_chunk = static_cast<long long>(batch) * C;
+  if (per_chunk > kNoAllocGnEntries)
+    return fail(LDB_ERR_SHAPE,
+                "group_norm_affine_noalloc: batch * channels = %lld exceeds the fixed scratch of %lld entries",
+                per_chunk, kNoAllocGnEntries);
+  const int nchunks = static_cast<int>(std::min<long long>(gn_chunks(voxels, batch), kNoAllocGnEntries / per_chunk));
+  float2* partials = nullptr;
+  rc = noalloc_scratch(&partials);
+  if (rc != LDB_OK) return rc;
+  const int vecs = C / 8;
+  int threads = 256;
+  if (vecs > threads) threads = ((vecs + 31) / 32) * 32;
+  threads = std::min(threads, 1024);
+  if (vecs > threads) return fail(LDB_ERR_SHAPE, "too many channels for one block row");
+  const int rows = threads / vecs;
+  const size_t smem = static_cast<size_t>(rows) * C * 2 * sizeof(float);
+  if (smem > 200 * 1024) return fail(LDB_ERR_SHAPE, "group norm reduction exceeds shared memory");
+  if (smem > 48 * 1024) {
+    static unsigned long long configured = 0;
+    rc = ensure_smem_attribute(reinterpret_cast<const void*>(gn_partial_kernel), 200 * 1024, &configured,
+                               "gn smem attribute");
+    if (rc != LDB_OK) return rc;
+  }
+  const int chunk_voxels = (voxels + nchunks - 1) / nchunks;
+  gn_partial_kernel<<<dim3(nchunks, batch), threads, smem, stream>>>(s, voxels, chunk_voxels, partials, nchunks);
+  count_launch();
+  rc = check_cuda(cudaGetLastError(), "gn_partial (noalloc) launch");
+  if (rc != LDB_OK) return rc;
+  gn_finalize_kernel<<<batch * groups, 128, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
+                                                         affine);
+  count_launch();
+  return check_cuda(cudaGetLastError(), "gn_finalize (noalloc) launch");
 }
 
 }  // extern "C"
