@@ -357,6 +357,7 @@ def main() -> None:
                           "flops_per_step": attn["flops"], "ms_per_step": attn["ms"], "launches": attn["launches"]},
             "e2e": {"value": e_value, "unit": UNIT, "h2d_bytes_per_step": int(host_noise.numel() * 4),
                     "d2h_bytes_per_step": int(host_out.numel() * 4)},
+            "kernel_ms_per_step": {k: round(v["ms"], 4) for k, v in sorted(kernel.items())},
             "gpu_launches": int(launches_per_step * args.steps),
             "launches_per_step": int(launches_per_step),
             "clocks": clock_info,

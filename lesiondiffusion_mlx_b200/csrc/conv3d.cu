@@ -8,9 +8,13 @@
 // zero fill supplies the padding.  Weights are packed K-major
 // [parity][Cout][tap][Cin] and loaded as 2-D TMA tiles.  A single thread of
 // the MMA warp issues tcgen05.mma (M=128, N=BN, K=16) into a double-buffered
-// TMEM accumulator; four epilogue warps drain TMEM (tcgen05.ld), add bias,
-// per-batch shift, output scale, residual, optional GELU, round once and
-// store NDHWC.  The kernel is persistent: CTA i walks tiles i, i+grid, ...
+// TMEM accumulator; four epilogue warps drain TMEM (tcgen05.ld) in chunks of
+// 128 output bytes per row, add bias + per-batch shift (staged once per
+// tile in shared memory), scale, the residual (prefetched by TMA into
+// shared memory), optional GELU, round once, write the chunk into a
+// swizzled staging buffer and store it with one TMA tensor store (the
+// folded upsampling conv stores through 8 output-parity views).  The kernel
+// is persistent: CTA i walks tiles i, i+grid, ...
 //
 // FP32 "exact" mode follows the reference's split (hi = f16(v), lo =
 // f16((v - hi) * 2^11)): per K step it issues hi*hi into one accumulator and
@@ -169,18 +173,193 @@ struct ConvCfg {
   static constexpr int kBBytesRaw = BN * KC * 2;
   static constexpr int kBBytes = ((kBBytesRaw + 1023) / 1024) * 1024;
   static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
-  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  // Epilogue staging: 2 output + 2 residual buffers of 128 rows x 128 bytes.
+  static constexpr int kEpiBufBytes = kTileM * 128;
+  static constexpr int kEpiBytes = 4 * kEpiBufBytes;
+  static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * kPlanes;
   static constexpr int kTmemColsRaw = 2 * kAccCols;
   static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
-  static constexpr int kChunk = BN < 32 ? BN : 32;
+  // Output element size (f32 in exact mode, f16 otherwise) and the columns
+  // per epilogue chunk: one 128-byte row (at most BN).
+  static constexpr int kOutBytes = EXACT ? 4 : 2;
+  static constexpr int kOutChunk = (128 / kOutBytes) < BN ? (128 / kOutBytes) : BN;
+  static constexpr int kPartChunk = 32 < BN ? 32 : BN;  // split-K partials are f32
   static constexpr uint32_t kIdesc = make_idesc_f16(kTileM, BN, 0, 0, 0);
-  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain
-  static constexpr int kBarrierBytes = (2 * kStages + 5) * 8;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + kBarrierBytes + 64;
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, res_full[2]
+  static constexpr int kBarrierBytes = (2 * kStages + 7) * 8;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kEpiBytes + 1024 /*align slack*/ + kBarrierBytes + 64 + BN * 4;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
 };
+
+// Per-thread state of the epilogue warps, carried across tiles.
+struct EpiState {
+  uint8_t* epi;          // out staging [2] then residual staging [2], 128 rows x 128 B each
+  uint64_t* res_full;    // [2]
+  float* bsum;           // [BN]
+  volatile int* abort_flag;
+  unsigned int* status;
+  int quarter, row;
+  bool leader;
+  uint32_t oq = 0;               // output chunks issued (staging buffer parity)
+  uint32_t rq = 0;               // residual chunks consumed
+  uint32_t res_uses0 = 0;        // completed phases of residual buffer 0
+  uint32_t res_uses1 = 0;        // ... and of buffer 1
+};
+
+// One output tile: wait for its accumulator, then per chunk of CC columns
+// TMEM -> registers -> (bias + shift) * scale + residual -> GELU -> round ->
+// swizzled staging row -> one TMA store by the leader.  With SPLIT the raw
+// f32 partial sums are stored instead (the reduce kernel applies the rest).
+template <class Cfg, int BN, bool EXACT, int CC, bool SPLIT>
+__device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMaps& maps, const TileCoord& c,
+                                              uint32_t tbase, uint64_t* acc_full_bar, uint32_t acc_parity,
+                                              EpiState& st) {
+  constexpr int kElem = SPLIT ? 4 : Cfg::kOutBytes;
+  constexpr uint32_t kRowBytes = CC * kElem;  // 32, 64 or 128
+  constexpr int kPerUnit = 16 / kElem;        // elements per 16-byte unit
+  constexpr int kChunks = BN / CC;
+  const int et = threadIdx.x - 64;
+  const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
+  const int omap = p.mode == kConvUp2 ? c.par : 0;
+  const int n0 = c.nt * BN;
+  const bool has_res = !SPLIT && p.residual != nullptr;
+  const uint32_t res_bytes = kRowBytes * static_cast<uint32_t>(p.bw * p.bh * p.bd);
+  uint8_t* const res_base = st.epi + 2 * Cfg::kEpiBufBytes;  // residual buffer rb at res_base + rb * kEpiBufBytes
+  if (has_res && st.leader) {
+    // prefetch the residual of chunk 0 while the tile's MMAs still run
+    const int rb = st.rq & 1;
+    mbar_arrive_expect_tx(&st.res_full[rb], res_bytes);
+    tma_load_5d(res_base + rb * Cfg::kEpiBufBytes, &maps.r[omap], &st.res_full[rb], n0, w0, h0, d0, c.b);
+  }
+  // Never leave early: the four epilogue warps must reach the same sequence
+  // of named barriers.  After a timeout the waits below fail fast (the abort
+  // flag is set) and the tile is written with whatever TMEM holds.
+  bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
+  tc_fence_after();
+  if (!SPLIT) {
+    for (int j = et; j < BN; j += 128) {
+      const int col = n0 + j;
+      float add = 0.f;
+      if (col < p.cout) {
+        if (p.bias) add = p.bias[col];
+        if (p.shift) add += p.shift[static_cast<long long>(c.b) * p.cout + col];
+      }
+      st.bsum[j] = add;
+    }
+  }
+  named_barrier(1, 128);
+  const uint32_t rowoff = static_cast<uint32_t>(st.row) * kRowBytes;
+#pragma unroll 1
+  for (int q = 0; q < kChunks; ++q) {
+    uint8_t* ob = st.epi + (st.oq & 1) * Cfg::kEpiBufBytes;
+    if (st.leader) {
+      bulk_wait_group_read<1>();  // the store issued two chunks ago has read this buffer
+      if (has_res && q + 1 < kChunks) {
+        const int rb = (st.rq + 1) & 1;
+        mbar_arrive_expect_tx(&st.res_full[rb], res_bytes);
+        tma_load_5d(res_base + rb * Cfg::kEpiBufBytes, &maps.r[omap], &st.res_full[rb], n0 + (q + 1) * CC, w0, h0,
+                    d0, c.b);
+      }
+    }
+    named_barrier(1, 128);
+    const int c0 = q * CC;
+    float v[CC];
+#pragma unroll
+    for (int s16 = 0; s16 < CC / 16; ++s16) {
+      uint32_t r[16];
+      tmem_ld16(tbase + c0 + s16 * 16, r);
+      if constexpr (EXACT) {
+        uint32_t lo[16];
+        tmem_ld16(tbase + BN + c0 + s16 * 16, lo);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          v[s16 * 16 + j] = __uint_as_float(r[j]) + __uint_as_float(lo[j]) * (1.0f / 2048.0f);
+      } else {
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[s16 * 16 + j] = __uint_as_float(r[j]);
+      }
+    }
+    if constexpr (SPLIT) {
+#pragma unroll
+      for (int u = 0; u < CC / 4; ++u) {
+        *reinterpret_cast<float4*>(ob + swizzle_offset(rowoff + u * 16, kRowBytes)) =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+      }
+    } else {
+      const uint8_t* rbuf = nullptr;
+      if (has_res) {
+        const int rb = st.rq & 1;
+        uint32_t& uses = rb ? st.res_uses1 : st.res_uses0;
+        if (!mbar_wait(&st.res_full[rb], uses & 1, st.abort_flag, st.status)) ok = false;
+        uses += 1;
+        st.rq += 1;
+        rbuf = res_base + rb * Cfg::kEpiBufBytes;
+      }
+#pragma unroll
+      for (int u = 0; u < CC / kPerUnit; ++u) {
+        const uint32_t off = swizzle_offset(rowoff + u * 16, kRowBytes);
+        float y[kPerUnit];
+#pragma unroll
+        for (int j = 0; j < kPerUnit; ++j) y[j] = (v[u * kPerUnit + j] + st.bsum[c0 + u * kPerUnit + j]) * p.out_scale;
+        if (rbuf) {
+          if constexpr (EXACT) {
+            const float4 rr = *reinterpret_cast<const float4*>(rbuf + off);
+            y[0] += rr.x;
+            y[1] += rr.y;
+            y[2] += rr.z;
+            y[3] += rr.w;
+          } else {
+            const uint4 raw = *reinterpret_cast<const uint4*>(rbuf + off);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __half22float2(h2[j]);
+              y[2 * j] += f.x;
+              y[2 * j + 1] += f.y;
+            }
+          }
+        }
+        if (p.act == kActGelu) {
+#pragma unroll
+          for (int j = 0; j < kPerUnit; ++j) {
+            // The reference rounds the dense output to the activation dtype
+            // before its FP32 GELU (mlx_model.py:369-374 after :204-217).
+            const float z = EXACT ? y[j] : __half2float(__float2half_rn(y[j]));
+            y[j] = gelu_erf_f32(z);
+          }
+        }
+        if constexpr (EXACT) {
+          *reinterpret_cast<float4*>(ob + off) = make_float4(y[0], y[1], y[2], y[3]);
+        } else {
+          uint4 raw;
+          __half2* h2 = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+          *reinterpret_cast<uint4*>(ob + off) = raw;
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    named_barrier(1, 128);
+    if (st.leader) {
+      if constexpr (SPLIT) {
+        const int prow = (c.ks * (p.num_tiles / p.k_splits) + c.out_tile) * kTileM;
+        tma_store_2d(&maps.part, ob, c0, prow);
+      } else {
+        tma_store_5d(&maps.o[omap], ob, n0 + c0, w0, h0, d0, c.b);
+      }
+      bulk_commit_group();
+    }
+    st.oq += 1;
+  }
+  return ok;
+}
 
 template <int KC, int BN, bool EXACT>
 __global__ void __launch_bounds__(kConvThreads, 1)
@@ -189,13 +368,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   using Cfg = ConvCfg<KC, BN, EXACT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint8_t* epi = smem + Cfg::kStages * Cfg::kStageBytes;  // out[2] | res[2], 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + Cfg::kEpiBytes);
   uint64_t* empty = full + Cfg::kStages;
   uint64_t* acc_full = empty + Cfg::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_full = drain + 1;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* bsum = reinterpret_cast<float*>(tmem_slot + 16);  // [BN] bias + shift of the current tile
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -210,6 +392,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_init(&acc_empty[a], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(&res_full[0], 1);
+    mbar_init(&res_full[1], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -217,6 +401,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tma_prefetch_desc(&wmap);
     const int nmaps = p.mode == kConv3x3x3S2 ? 8 : 1;
     for (int i = 0; i < nmaps; ++i) tma_prefetch_desc(&maps.a[i]);
+  }
+  if (warp == 2 && lane == 0) {
+    const int nout = p.mode == kConvUp2 ? 8 : 1;
+    if (p.k_splits > 1) {
+      tma_prefetch_desc(&maps.part);
+    } else {
+      for (int i = 0; i < nout; ++i) tma_prefetch_desc(&maps.o[i]);
+      if (p.residual)
+        for (int i = 0; i < nout; ++i) tma_prefetch_desc(&maps.r[i]);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -350,51 +544,33 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const int row = quarter * 32 + lane;
+    EpiState st;
+    st.epi = epi;
+    st.res_full = res_full;
+    st.bsum = bsum;
+    st.abort_flag = abort_flag;
+    st.status = status;
+    st.quarter = warp & 3;
+    st.row = st.quarter * 32 + lane;
+    st.leader = threadIdx.x == 64;
+    const bool split = p.k_splits > 1;
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const TileCoord c = decode_tile(p, t);
       const int acc = local & 1;
-      if (!warp_wait(&acc_full[acc], (local >> 1) & 1, abort_flag, status)) break;
-      tc_fence_after();
-      const long long voxel = row_voxel(p, c, row);
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * Cfg::kAccCols;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += Cfg::kChunk) {
-        float v[Cfg::kChunk];
-        {
-          uint32_t r[Cfg::kChunk];
-          if constexpr (Cfg::kChunk == 32) tmem_ld32(tbase + c0, r);
-          else tmem_ld16(tbase + c0, r);
-          if constexpr (EXACT) {
-            uint32_t q[Cfg::kChunk];
-            if constexpr (Cfg::kChunk == 32) tmem_ld32(tbase + BN + c0, q);
-            else tmem_ld16(tbase + BN + c0, q);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < Cfg::kChunk; ++j)
-              v[j] = __uint_as_float(r[j]) + __uint_as_float(q[j]) * (1.0f / 2048.0f);
-          } else {
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < Cfg::kChunk; ++j) v[j] = __uint_as_float(r[j]);
-          }
-        }
-        const int col = c.nt * BN + c0;
-        if (p.k_splits > 1) {
-          float* dst = p.partials + ((static_cast<long long>(c.ks) * (p.num_tiles / p.k_splits) + c.out_tile) * kTileM + row) * BN + c0;
-#pragma unroll
-          for (int j = 0; j < Cfg::kChunk; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else if (voxel >= 0 && col < p.cout) {
-          store_outputs<Cfg::kChunk>(p, c.b, voxel, col, v);
-        }
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(st.quarter * 32) << 16) + acc * Cfg::kAccCols;
+      bool ok;
+      if (split) {
+        ok = epilogue_tile<Cfg, BN, EXACT, Cfg::kPartChunk, true>(p, maps, c, tbase, &acc_full[acc], (local >> 1) & 1, st);
+      } else {
+        ok = epilogue_tile<Cfg, BN, EXACT, Cfg::kOutChunk, false>(p, maps, c, tbase, &acc_full[acc], (local >> 1) & 1, st);
       }
+      (void)ok;  // a failed wait already raised the abort flag and the device status
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (st.leader) bulk_wait_group_all();  // stores must finish before the CTA releases its shared memory
   }
 
   __syncwarp();
@@ -625,6 +801,9 @@ int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x
     return fail(LDB_ERR_SHAPE, "res_ld %d < out_channels %d", desc->res_ld, desc->out_channels);
   if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
     return fail(LDB_ERR_WORKSPACE, "conv3d needs %zu workspace bytes, got %zu", plan.workspace, workspace_bytes);
+  if ((desc->exact != 0) != (desc->out_dtype == LDB_F32))
+    return fail(LDB_ERR_INVALID, "conv3d output dtype must be f32 in exact mode and f16 otherwise");
+  const ldb_conv_desc* d = desc;
   ConvParams& p = plan.p;
   p.bias = bias;
   p.shift = shift;
@@ -667,6 +846,58 @@ int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x
     rc = encode_tiled_f16(&maps.a[0], x, 5, dims, strides, abox, plan.kc * 2);
     if (rc != LDB_OK) return rc;
   }
+  // Output / residual store-load maps (or the split-K partial map).
+  const int out_esz = exact ? 4 : 2;
+  if (p.k_splits > 1) {
+    const int cc = std::min(plan.bn, 32);
+    const uint64_t dims[2] = {static_cast<uint64_t>(plan.bn), static_cast<uint64_t>(p.num_tiles) * kTileM};
+    const uint64_t strides[1] = {static_cast<uint64_t>(plan.bn) * 4};
+    const uint32_t box[2] = {static_cast<uint32_t>(cc), static_cast<uint32_t>(kTileM)};
+    rc = encode_tiled_f32(&maps.part, workspace, 2, dims, strides, box, cc * 4);
+    if (rc != LDB_OK) return rc;
+  } else {
+    const int cc = std::min(plan.bn, 128 / out_esz);
+    const uint32_t obox[5] = {static_cast<uint32_t>(cc), static_cast<uint32_t>(p.bw), static_cast<uint32_t>(p.bh),
+                              static_cast<uint32_t>(p.bd), 1u};
+    auto encode_out = [&](CUtensorMap* dst, const void* base_ptr, int ld) -> int {
+      if ((static_cast<long long>(ld) * out_esz) % 16 != 0)
+        return fail(LDB_ERR_ALIGNMENT, "output/residual channel stride %d is not a multiple of 16 bytes", ld);
+      const uint64_t lde = static_cast<uint64_t>(ld) * out_esz;
+      const int nviews = d->mode == LDB_CONV_UP2 ? 8 : 1;
+      for (int v = 0; v < nviews; ++v) {
+        uint64_t dims[5], strides[4];
+        const uint8_t* base = static_cast<const uint8_t*>(base_ptr);
+        if (nviews == 8) {
+          const int pd = v >> 2, ph = (v >> 1) & 1, pw = v & 1;
+          const uint64_t OW = p.out_w, OH = p.out_h, OD = p.out_d;
+          base += ((static_cast<uint64_t>(pd) * OH + ph) * OW + pw) * lde;
+          const uint64_t dd[5] = {static_cast<uint64_t>(p.cout), static_cast<uint64_t>(p.grid_w),
+                                  static_cast<uint64_t>(p.grid_h), static_cast<uint64_t>(p.grid_d),
+                                  static_cast<uint64_t>(p.batch)};
+          const uint64_t ss[4] = {2 * lde, 2 * OW * lde, 2 * OH * OW * lde, OD * OH * OW * lde};
+          memcpy(dims, dd, sizeof(dd));
+          memcpy(strides, ss, sizeof(ss));
+        } else {
+          const uint64_t OW = p.out_w, OH = p.out_h, OD = p.out_d;
+          const uint64_t dd[5] = {static_cast<uint64_t>(p.cout), OW, OH, OD, static_cast<uint64_t>(p.batch)};
+          const uint64_t ss[4] = {lde, OW * lde, OH * OW * lde, OD * OH * OW * lde};
+          memcpy(dims, dd, sizeof(dd));
+          memcpy(strides, ss, sizeof(ss));
+        }
+        const int r = exact ? encode_tiled_f32(&dst[v], base, 5, dims, strides, obox, cc * out_esz)
+                            : encode_tiled_f16(&dst[v], base, 5, dims, strides, obox, cc * out_esz);
+        if (r != LDB_OK) return r;
+      }
+      return LDB_OK;
+    };
+    rc = encode_out(maps.o, out, desc->out_ld);
+    if (rc != LDB_OK) return rc;
+    if (residual) {
+      rc = encode_out(maps.r, residual, desc->res_ld);
+      if (rc != LDB_OK) return rc;
+    }
+  }
+
   CUtensorMap wmap;
   const uint64_t ktotal = static_cast<uint64_t>(plan.taps) * plan.cin_pad * (exact ? 2 : 1);
   const uint64_t wrows = static_cast<uint64_t>(p.parities) * p.wrows_per_parity;

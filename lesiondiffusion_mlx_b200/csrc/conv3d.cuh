@@ -51,10 +51,15 @@ struct ConvParams {
   int out_d, out_h, out_w;
 };
 
-// Up to 8 activation tensor maps: one for plain modes, 8 parity views for
-// stride 2.
+// Tensor maps of one convolution: activation loads (one map, or 8 parity
+// views for stride 2), output stores and residual loads (one map, or the 8
+// output-parity views of the folded upsampling conv), and the split-K
+// partial-tile store.
 struct ConvMaps {
   CUtensorMap a[8];
+  CUtensorMap o[8];
+  CUtensorMap r[8];
+  CUtensorMap part;
 };
 
 }  // namespace ldb

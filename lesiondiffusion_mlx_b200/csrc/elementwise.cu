@@ -89,8 +89,10 @@ __global__ void dense_small_kernel(const __half* x, int x_ld, const __half* w, c
   }
 #pragma unroll
   for (int m = 0; m < kDenseMaxRows; ++m) {
+    if (m < rows) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    }
   }
   if (lane == 0) {
     const float b = bias ? bias[warp] : 0.f;

@@ -100,8 +100,25 @@ unsigned int* device_status_ptr() {
   return cache[dev];
 }
 
+namespace {
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
+}  // namespace
+
 int encode_tiled_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes, bool bf16) {
+  return encode_tiled(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, rank,
+                      dims, strides_bytes, box, swizzle_bytes);
+}
+
+int encode_tiled_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rank, dims, strides_bytes, box, swizzle_bytes);
+}
+
+namespace {
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(LDB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
@@ -126,13 +143,13 @@ int encode_tiled_f16(CUtensorMap* map, const void* base, int rank, const uint64_
   if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
   if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
   if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+  CUresult r = fn(map, type, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(LDB_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
   return LDB_OK;
 }
+}  // namespace
 
 }  // namespace ldb
 

@@ -44,4 +44,8 @@ int encode_tiled_f16(CUtensorMap* map, const void* base, int rank, const uint64_
                      const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes,
                      bool bf16 = false);
 
+// Same for 32-bit float elements.
+int encode_tiled_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
+
 }  // namespace ldb

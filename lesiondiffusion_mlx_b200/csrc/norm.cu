@@ -117,29 +117,60 @@ __global__ void gn_partial_kernel(Src2 s, int voxels, int chunk_voxels, float2* 
 }
 
 // One block per (batch, group): merge the per-channel partials in FP64 and
-// write the per-channel affine (scale, offset).
+// write the per-channel affine (scale, offset).  Threads split the
+// (chunk, channel) pairs of the group: with cpg <= 256 the block size is a
+// multiple of cpg, so each thread keeps one channel and strides over chunks
+// (consecutive threads read consecutive channels), then folds its sums into
+// shared memory.
 __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, int nchunks, int groups,
                                    const float* gamma, const float* beta, float eps, float* affine) {
   const int c_total = s.c1 + s.c2;
   const int cpg = c_total / groups;
   const int b = blockIdx.x / groups;
   const int g = blockIdx.x % groups;
-  __shared__ double sh_mean[1024];
-  __shared__ double sh_m2[1024];
+  __shared__ double sh_a[1024];
+  __shared__ double sh_q[1024];
   __shared__ double sh_gmean;
   __shared__ double sh_rstd;
   const double n = static_cast<double>(voxels);
-  // Channel statistics (one thread per channel of the group).
+  for (int j = threadIdx.x; j < cpg; j += blockDim.x) {
+    sh_a[j] = 0.0;
+    sh_q[j] = 0.0;
+  }
+  __syncthreads();
+  const float2* base = partials + static_cast<long long>(b) * nchunks * c_total + g * cpg;
+  if (cpg <= static_cast<int>(blockDim.x)) {
+    const int lanes = (blockDim.x / cpg) * cpg;  // threads in use, a multiple of cpg
+    if (threadIdx.x < lanes) {
+      const int j = threadIdx.x % cpg;
+      const int k0 = threadIdx.x / cpg;
+      const int kstep = lanes / cpg;
+      double a = 0.0, q = 0.0;
+      for (int k = k0; k < nchunks; k += kstep) {
+        const float2 p = base[static_cast<long long>(k) * c_total + j];
+        a += p.x;
+        q += p.y;
+      }
+      atomicAdd(&sh_a[j], a);
+      atomicAdd(&sh_q[j], q);
+    }
+  } else {
+    for (int j = threadIdx.x; j < cpg; j += blockDim.x) {
+      double a = 0.0, q = 0.0;
+      for (int k = 0; k < nchunks; ++k) {
+        const float2 p = base[static_cast<long long>(k) * c_total + j];
+        a += p.x;
+        q += p.y;
+      }
+      sh_a[j] = a;
+      sh_q[j] = q;
+    }
+  }
+  __syncthreads();
+  // Channel means and centred sums of squares (shift = the channel's value at voxel 0).
+  const long long v0 = static_cast<long long>(b) * voxels;
   for (int j = threadIdx.x; j < cpg; j += blockDim.x) {
     const int c = g * cpg + j;
-    double a = 0.0, q = 0.0;
-    for (int k = 0; k < nchunks; ++k) {
-      const float2 p = partials[(static_cast<long long>(b) * nchunks + k) * c_total + c];
-      a += p.x;
-      q += p.y;
-    }
-    // shift of this channel = value at voxel 0
-    const long long v0 = static_cast<long long>(b) * voxels;
     double shift;
     if (c < s.c1) {
       shift = s.f32 ? static_cast<const float*>(s.x1)[v0 * s.ld1 + c]
@@ -149,19 +180,21 @@ __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, i
       shift = s.f32 ? static_cast<const float*>(s.x2)[v0 * s.ld2 + cc]
                     : __half2float(static_cast<const __half*>(s.x2)[v0 * s.ld2 + cc]);
     }
+    const double a = sh_a[j];
     const double mean_shifted = a / n;
-    sh_mean[j] = shift + mean_shifted;
-    sh_m2[j] = fmax(q - a * mean_shifted, 0.0);
+    const double m2 = fmax(sh_q[j] - a * mean_shifted, 0.0);
+    sh_a[j] = shift + mean_shifted;
+    sh_q[j] = m2;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     double gm = 0.0;
-    for (int j = 0; j < cpg; ++j) gm += sh_mean[j];
+    for (int j = 0; j < cpg; ++j) gm += sh_a[j];
     gm /= cpg;
     double m2 = 0.0;
     for (int j = 0; j < cpg; ++j) {
-      const double d = sh_mean[j] - gm;
-      m2 += sh_m2[j] + n * d * d;
+      const double d = sh_a[j] - gm;
+      m2 += sh_q[j] + n * d * d;
     }
     const double var = m2 / (n * cpg);
     sh_gmean = gm;
@@ -202,15 +235,25 @@ __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_ba
   uint4 hi_raw, lo_raw;
   __half* hi = reinterpret_cast<__half*>(&hi_raw);
   __half* lo = reinterpret_cast<__half*>(&lo_raw);
+  float sc[8], of[8];
+  if (affine && c + 8 <= c_total) {
+    // 8 (scale, offset) pairs = four 16-byte loads
+    const float4* a4 = reinterpret_cast<const float4*>(affine + (static_cast<long long>(b) * c_total + c) * 2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 t = a4[q];
+      sc[2 * q] = t.x;
+      of[2 * q] = t.y;
+      sc[2 * q + 1] = t.z;
+      of[2 * q + 1] = t.w;
+    }
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float y = 0.f;
     if (c + j < c_total) {
       y = v[j];
-      if (affine) {
-        const float* a = affine + (static_cast<long long>(b) * c_total + c + j) * 2;
-        y = fmaf(y, a[0], a[1]);
-      }
+      if (affine) y = fmaf(y, sc[j], of[j]);
       if (silu) y = silu_f32(y);
     }
     hi[j] = __float2half_rn(y);
@@ -392,7 +435,7 @@ int ldb_group_norm_affine(cudaStream_t stream, const void* x1, int c1, int ld1, 
   count_launch();
   rc = check_cuda(cudaGetLastError(), "gn_partial launch");
   if (rc != LDB_OK) return rc;
-  gn_finalize_kernel<<<batch * groups, 128, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
+  gn_finalize_kernel<<<batch * groups, 256, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
                                                          affine);
   count_launch();
   return check_cuda(cudaGetLastError(), "gn_finalize launch");
@@ -484,7 +527,7 @@ int ldb_group_norm_affine_noalloc(cudaStream_t stream, const void* x1, int c1, i
   count_launch();
   rc = check_cuda(cudaGetLastError(), "gn_partial (noalloc) launch");
   if (rc != LDB_OK) return rc;
-  gn_finalize_kernel<<<batch * groups, 128, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
+  gn_finalize_kernel<<<batch * groups, 256, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
                                                          affine);
   count_launch();
   return check_cuda(cudaGetLastError(), "gn_finalize (noalloc) launch");

@@ -154,6 +154,24 @@ class LdmUnetB200(_Layers):
         self.in_channels = int(weights["input_blocks.0.0.weight"].shape[1])
         self.out_channels = int(weights["out.2.weight"].shape[0])
         self._pack_all()
+        self._stack_embedding_projections()
+
+    def _stack_embedding_projections(self) -> None:
+        """Stack every residual block's ``emb_layers.1`` so one skinny GEMM per step
+        produces all per-block shifts (they all read the same ``silu(emb)``)."""
+        keys = sorted(n[: -len(".emb_layers.1.weight")] for n in self.p.raw if n.endswith(".emb_layers.1.weight"))
+        offsets: dict[str, tuple[int, int]] = {}
+        weights, biases, start = [], [], 0
+        for key in keys:
+            w = self.p.raw[key + ".emb_layers.1.weight"]
+            n = int(w.shape[0])
+            offsets[key] = (start, start + n)
+            weights.append(w.to(torch.float16))
+            biases.append(self.p.raw[key + ".emb_layers.1.bias"].to(torch.float16).to(torch.float32))
+            start += n
+        self._emb_offsets = offsets
+        self._emb_weight = torch.cat(weights).to(self.device).contiguous()
+        self._emb_bias = torch.cat(biases).to(self.device).contiguous()
 
     def _pack_all(self) -> None:
         """Pack every weight now so a captured step holds no packing work."""
@@ -180,12 +198,19 @@ class LdmUnetB200(_Layers):
         h = ops.dense_small(emb, self.p.f16("time_embed.0.weight"), self.p.f32("time_embed.0.bias"))
         return ops.dense_small(h, self.p.f16("time_embed.2.weight"), self.p.f32("time_embed.2.bias"), in_silu=True)
 
+    def block_shifts(self, emb: torch.Tensor) -> torch.Tensor:
+        """All residual blocks' ``dense(silu(emb), emb_layers.1)`` in one launch, f16-rounded f32."""
+        return ops.dense_small(emb, self._emb_weight, self._emb_bias, in_silu=True, out_dtype=torch.float32,
+                               round_f16=True)
+
     def residual(self, x: torch.Tensor, emb: torch.Tensor, key: str, x2: torch.Tensor | None = None) -> torch.Tensor:
-        """mlx_model.py:420-441 (with the skip concatenation [x | x2] fused into the norm pass)."""
+        """mlx_model.py:420-441 (with the skip concatenation [x | x2] fused into the norm pass).
+
+        ``emb`` is the stacked per-block shift table from ``block_shifts``."""
         channels = int(x.shape[-1]) + (0 if x2 is None else int(x2.shape[-1]))
         groups = 32 if channels % 32 == 0 else channels
-        shift = ops.dense_small(emb, self.p.f16(key + ".emb_layers.1.weight"), self.p.f32(key + ".emb_layers.1.bias"),
-                                in_silu=True, out_dtype=torch.float32, round_f16=True)
+        lo, hi = self._emb_offsets[key]
+        shift = emb[:, lo:hi].contiguous()
         h = self.norm_silu_conv(x, key + ".in_layers.0", key + ".in_layers.2", groups=groups, eps=1e-5,
                                 shift=shift, x2=x2)
         out_c = int(h.shape[-1])
@@ -254,7 +279,7 @@ class LdmUnetB200(_Layers):
                 ) -> torch.Tensor:
         """Noise prediction for NDHWC f16 ``x`` (B, D, H, W, C_in) (mlx_model.py:599-654)."""
         cfg = self.config
-        emb = self.time_embedding(timesteps, step)
+        emb = self.block_shifts(self.time_embedding(timesteps, step))
         h = self.conv(x, "input_blocks.0.0")
         skips = [h]
         block, resolution = 1, 1

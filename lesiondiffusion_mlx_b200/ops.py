@@ -62,10 +62,11 @@ def group_norm_affine(
     affine = torch.empty((batch, channels, 2), dtype=torch.float32, device=x.device)
     g = None if gamma is None else gamma.to(torch.float32).contiguous()
     b = None if beta is None else beta.to(torch.float32).contiguous()
-    _lib.call(
-        "ldb_group_norm_affine", _stream(x), x.data_ptr(), c1, ld1, _ptr(x2), c2, ld2, _DT[x.dtype], batch, voxels,
-        groups, _ptr(g), _ptr(b), float(eps), affine.data_ptr(), workspace.data_ptr(), ws.value,
-    )
+    with instrument.maybe_time("group_norm", 0.0):
+        _lib.call(
+            "ldb_group_norm_affine", _stream(x), x.data_ptr(), c1, ld1, _ptr(x2), c2, ld2, _DT[x.dtype], batch,
+            voxels, groups, _ptr(g), _ptr(b), float(eps), affine.data_ptr(), workspace.data_ptr(), ws.value,
+        )
     return affine
 
 
@@ -92,10 +93,11 @@ def prepare_input(
     if out is None:
         out = torch.empty((*lead, width), dtype=torch.float16, device=x.device)
     _, _, out_ld = _rows(out)
-    _lib.call(
-        "ldb_prepare_input", _stream(x), x.data_ptr(), c1, ld1, _ptr(x2), c2, ld2, _DT[x.dtype], int(x.shape[0]),
-        voxels, _ptr(affine), int(silu), int(split), out.data_ptr(), out_ld,
-    )
+    with instrument.maybe_time("prepare", 0.0):
+        _lib.call(
+            "ldb_prepare_input", _stream(x), x.data_ptr(), c1, ld1, _ptr(x2), c2, ld2, _DT[x.dtype],
+            int(x.shape[0]), voxels, _ptr(affine), int(silu), int(split), out.data_ptr(), out_ld,
+        )
     return out if split else out[..., :channels]
 
 
@@ -109,8 +111,9 @@ def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: fl
     if out is None:
         out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
     _, _, out_ld = _rows(out)
-    _lib.call("ldb_layer_norm", _stream(x), x.data_ptr(), ld, gamma.data_ptr(), beta.data_ptr(), float(eps),
-              out.data_ptr(), out_ld, rows, c)
+    with instrument.maybe_time("layer_norm", 0.0):
+        _lib.call("ldb_layer_norm", _stream(x), x.data_ptr(), ld, gamma.data_ptr(), beta.data_ptr(), float(eps),
+                  out.data_ptr(), out_ld, rows, c)
     return out
 
 
@@ -164,10 +167,12 @@ def dense_small(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     n = int(weight.shape[0])
     if out is None:
         out = torch.empty((rows, n), dtype=out_dtype, device=x.device)
-    _lib.call(
-        "ldb_dense_small", _stream(x), x.data_ptr(), int(x.stride(0)), weight.data_ptr(), _ptr(bias), out.data_ptr(),
-        int(out.stride(0)), rows, n, k, int(in_silu), int(out_silu), _DT[out.dtype], int(round_f16),
-    )
+    with instrument.maybe_time("dense_small", 0.0):
+        _lib.call(
+            "ldb_dense_small", _stream(x), x.data_ptr(), int(x.stride(0)), weight.data_ptr(), _ptr(bias),
+            out.data_ptr(), int(out.stride(0)), rows, n, k, int(in_silu), int(out_silu), _DT[out.dtype],
+            int(round_f16),
+        )
     return out
 
 
@@ -189,11 +194,12 @@ def sampler_step(
     in_ld = 0
     if net_in is not None:
         _, _, in_ld = _rows(net_in)
-    _lib.call(
-        "ldb_sampler_step", _stream(x), kind, x.data_ptr(), _ptr(prev), _ptr(eps), eps_ld, _ptr(noise),
-        int(noise_step_stride), _ptr(mask), _ptr(image), image_c, _ptr(net_in), in_ld, batch, voxels, channels,
-        _ptr(coeff), _ptr(step),
-    )
+    with instrument.maybe_time("sampler_step", 0.0):
+        _lib.call(
+            "ldb_sampler_step", _stream(x), kind, x.data_ptr(), _ptr(prev), _ptr(eps), eps_ld, _ptr(noise),
+            int(noise_step_stride), _ptr(mask), _ptr(image), image_c, _ptr(net_in), in_ld, batch, voxels,
+            channels, _ptr(coeff), _ptr(step),
+        )
 
 
 def vq_nearest4(z: torch.Tensor, codebook: torch.Tensor, *, quantized: torch.Tensor | None = None) -> torch.Tensor:
