@@ -3,17 +3,22 @@
 // cross-attention to the projected text context, in the projection layout
 // (B, L, H*D) of lesiondiffusion_mlx/_attention*.py (no head transposes).
 //
-// One CTA owns 128 queries of one (batch, head).  Warp 0 streams Q once and
-// K/V blocks of 128 keys by TMA (2 stages); warp 1 issues S = Q K^T into one
-// of two TMEM score buffers and O += P V (P from shared memory, V as an
-// MN-major operand); warps 2-5 each own 32 query rows (one TMEM lane per
-// thread) and run the online softmax: FP32 scores and running max / sum,
-// probabilities rounded to the input type for the PV product, the FP32
-// output rescaled in TMEM when the running max grows, and the final O / l
-// rounded once -- the contract of _attention_half.py:58-113.  Keys past Lk
-// get probability 0 (cross-attention to 77 tokens uses one partial block).
-// The score buffers are double-buffered, so Q K^T of block j+1 runs on the
-// tensor cores while the softmax of block j runs on the CUDA cores.
+// One CTA owns two 128-query tiles of one (batch, head) and streams K/V
+// blocks of 128 keys once for both.  Warp 0 issues the TMA loads (Q once,
+// K/V in a 3-stage ring); warp 1 issues the MMAs: S_t = Q_t K^T into a TMEM
+// score buffer per tile and O_t += P_t V (P from shared memory, V as an
+// MN-major operand).  Warps 2-5 run the online softmax of tile 0 and warps
+// 6-9 that of tile 1, one query row per thread: while one warpgroup turns
+// its scores into probabilities, the tensor core works on the other tile.
+//
+// Softmax contract of _attention_half.py:58-113: FP32 scores, running max
+// and sum; probabilities rounded to the input type for the PV product; the
+// FP32 output divided by the sum and rounded once.  The running output is
+// rescaled lazily: a row keeps its reference maximum until a new maximum
+// exceeds it by more than 2^8 in probability, so probabilities stay within
+// [0, 256] (exact in f16/bf16 range) and most blocks skip the TMEM rescale.
+// Keys past Lk get probability 0 (cross-attention to 77 tokens is one
+// partial block).
 
 #include <algorithm>
 #include <cstring>
@@ -24,9 +29,10 @@
 namespace ldb {
 namespace {
 
-constexpr int kAttnThreads = 192;
-constexpr int kBlockM = 128;
-constexpr int kBlockN = 128;
+constexpr int kAttnThreads = 320;  // producer, MMA, 2 x 4 softmax warps
+constexpr int kBlockM = 128;       // queries per tile (two tiles per CTA)
+constexpr int kBlockN = 128;       // keys per block
+constexpr float kRescaleLog2 = 8.0f;
 
 template <int D>
 struct AttnCfg {
@@ -36,18 +42,18 @@ struct AttnCfg {
   static constexpr int kQBytes = kBlockM * kRowBytes;
   static constexpr int kKBytes = kBlockN * kRowBytes;
   static constexpr int kPBytes = kBlockM * kBlockN * 2;  // two 64-key SW128 chunks
-  static constexpr int kStages = 2;
-  // smem: Q | K0 V0 | K1 V1 | P | barriers
-  static constexpr int kOffK = kQBytes;
-  static constexpr int kOffP = kQBytes + kStages * 2 * kKBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
+  static constexpr int kStages = 3;
+  // smem: Q0 Q1 | (K V) x stages | P0 P1 | barriers
+  static constexpr int kOffK = 2 * kQBytes;
+  static constexpr int kOffP = kOffK + kStages * 2 * kKBytes;
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-  static constexpr int kTmemCols = 512;  // S0: [0,128), S1: [128,256), O: [256, 256 + D)
+  static constexpr int kTmemCols = 512;  // S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [384, 384+D)
 };
 
 struct AttnParams {
   int batch, heads, lq, lk;
-  int out_ld;       // elements between output rows
+  int out_ld;        // elements between output rows
   float scale_log2;  // softmax scale * log2(e)
   void* out;
 };
@@ -62,35 +68,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_ready = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars + 1;    // [3]
+  uint64_t* kv_empty = bars + 4;   // [3]
+  uint64_t* s_full = bars + 7;     // [2] per query tile
+  uint64_t* p_ready = bars + 9;    // [2]
+  uint64_t* pv_done = bars + 11;   // [2]
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int q0 = blockIdx.x * kBlockM;
+  const int q0 = blockIdx.x * 2 * kBlockM;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int nblocks = (p.lk + kBlockN - 1) / kBlockN;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&pv_done[t], 1);
     }
-    mbar_init(p_ready, 4);
-    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -108,20 +112,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
-
-  uint8_t* sq = smem;
-  uint8_t* sp = smem + Cfg::kOffP;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t armed_mask = 0, armed_parity = 0;
-      mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
-      tma_load_3d(sq, &qmap, q_full, h * D, q0, b);
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
+      tma_load_3d(smem, &qmap, q_full, h * D, q0, b);
+      tma_load_3d(smem + Cfg::kQBytes, &qmap, q_full, h * D, q0 + kBlockM, b);
       for (int j = 0; j < nblocks; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % Cfg::kStages;
+        const uint32_t ph = (j / Cfg::kStages) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status)) break;
         uint8_t* sk = smem + Cfg::kOffK + st * 2 * Cfg::kKBytes;
         mbar_arrive_expect_tx(&kv_full[st], 2 * Cfg::kKBytes);
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (*abort_flag) {
         volatile int never = 0;
         mbar_wait(q_full, 0, &never, status);
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < Cfg::kStages; ++s)
           if (armed_mask & (1u << s)) mbar_wait(&kv_full[s], (armed_parity >> s) & 1u, &never, status);
       }
     }
@@ -142,41 +143,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kBlockM, kBlockN, BF16 ? 1u : 0u, 0u, 0u);
       constexpr uint32_t idesc_pv = make_idesc_f16(kBlockM, D, BF16 ? 1u : 0u, 0u, 1u);
-      const uint32_t q_addr = smem_u32(sq);
-      const uint32_t p_addr = smem_u32(sp);
       bool ok = mbar_wait(q_full, 0, abort_flag, status);
       for (int j = 0; ok && j <= nblocks; ++j) {
-        if (j < nblocks) {
-          // S_j = Q K_j^T into score buffer j & 1 once the softmax released it.
-          const int st = j & 1;
-          if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, status)) break;
-          if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1, abort_flag, status)) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * 2 * Cfg::kKBytes);
+        const int st = j % Cfg::kStages;
+        const int pst = (j + Cfg::kStages - 1) % Cfg::kStages;  // stage of block j - 1
+        if (j < nblocks && !mbar_wait(&kv_full[st], (j / Cfg::kStages) & 1, abort_flag, status)) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j > 0) {
+            // P_t(j-1) is in shared memory (and S_t is free): O_t += P_t V_{j-1}.
+            if (!mbar_wait(&p_ready[t], (j - 1) & 1, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t p_addr = smem_u32(smem + Cfg::kOffP + t * Cfg::kPBytes);
+            const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + pst * 2 * Cfg::kKBytes + Cfg::kKBytes);
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t ad = make_smem_desc(q_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-            const uint64_t bd = make_smem_desc(k_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-            umma_ss(tmem + st * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+            for (int k = 0; k < kBlockN / 16; ++k) {
+              const uint64_t ad = make_smem_desc(p_addr + (k >> 2) * (kBlockM * 128) + (k & 3) * 32, 16, 1024,
+                                                 kSwizzle128);
+              const uint64_t bd = make_smem_desc(v_addr + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8,
+                                                 Cfg::kSbo, Cfg::kLayout);
+              umma_ss(tmem + 256 + t * 128, ad, bd, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&pv_done[t]);
+            if (t == 1) umma_commit(&kv_empty[pst]);
           }
-          umma_commit(&s_full[st]);
-        }
-        if (j > 0) {
-          // P_{j-1} is in shared memory: O += P_{j-1} V_{j-1}.
-          if (!mbar_wait(p_ready, (j - 1) & 1, abort_flag, status)) break;
-          tc_fence_after();
-          const int st = (j - 1) & 1;
-          const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + st * 2 * Cfg::kKBytes + Cfg::kKBytes);
+          if (j < nblocks) {
+            // S_t(j) = Q_t K_j^T
+            const uint32_t q_addr = smem_u32(smem + t * Cfg::kQBytes);
+            const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * 2 * Cfg::kKBytes);
 #pragma unroll
-          for (int k = 0; k < kBlockN / 16; ++k) {
-            const uint64_t ad = make_smem_desc(p_addr + (k >> 2) * (kBlockM * 128) + (k & 3) * 32, 16, 1024,
-                                               kSwizzle128);
-            const uint64_t bd = make_smem_desc(v_addr + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8, Cfg::kSbo,
-                                               Cfg::kLayout);
-            umma_ss(tmem_o, ad, bd, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < D / 16; ++k) {
+              const uint64_t ad = make_smem_desc(q_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+              const uint64_t bd = make_smem_desc(k_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+              umma_ss(tmem + t * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t]);
           }
-          umma_commit(pv_done);
-          umma_commit(&kv_empty[st]);
         }
       }
       umma_commit(drain);
@@ -185,68 +189,79 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int quarter = warp & 3;   // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tmem_s = tmem + t * 128 + lane_base;
+    const uint32_t tmem_o = tmem + 256 + t * 128 + lane_base;
+    uint8_t* sp = smem + Cfg::kOffP + t * Cfg::kPBytes;
     const float c = p.scale_log2;
-    float m = -INFINITY;  // running max of raw scores
+    float m_ref = -INFINITY;  // reference maximum (raw scores) of the probabilities in O and l
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblocks; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, status)) {
+      if (!warp_wait(&s_full[t], j & 1, abort_flag, status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t tmem_s = tmem + sb * 128;
       const int valid = min(kBlockN, p.lk - j * kBlockN);
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBlockN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_s + lane_base + c0, r);
-        tmem_wait_ld();
+      uint32_t sr[kBlockN];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c0 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      for (int c0 = 0; c0 < kBlockN; c0 += 32) {
+        uint32_t(&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[c0]);
+        tmem_ld32(tmem_s + c0, chunk);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f((m - m_new) * c);
-      const float mc = m_new * c;
+      tmem_wait_ld();
+      float mx = -INFINITY;
+      if (valid == kBlockN) {
+#pragma unroll
+        for (int i = 0; i < kBlockN; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < kBlockN; ++i)
+          if (i < valid) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      }
+      const bool first = j == 0;
+      const bool grow = first || (mx - m_ref) * c > kRescaleLog2;
+      const float m_new = grow ? fmaxf(m_ref, mx) : m_ref;
+      const float alpha = first ? 0.f : exp2f((m_ref - m_new) * c);
       if (j > 0) {
-        // PV_{j-1} finished: the P buffer is free and O holds blocks < j.
-        if (!warp_wait(pv_done, (j - 1) & 1, abort_flag, status)) {
+        // PV_t(j-1) finished: the P buffer is free and O holds blocks < j.
+        if (!warp_wait(&pv_done[t], (j - 1) & 1, abort_flag, status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // tcgen05.ld/st are warp-collective: rescale the whole warp's rows
-        // when any of them saw a larger maximum (alpha == 1 elsewhere).
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
+        // tcgen05.ld/st are warp-collective: rescale the warp's rows when any grew.
+        if (__any_sync(0xffffffffu, grow)) {
+          const float scale = grow ? alpha : 1.f;
+#pragma unroll
           for (int c0 = 0; c0 < D; c0 += 16) {
             uint32_t r[16];
-            tmem_ld16(tmem_o + lane_base + c0, r);
+            tmem_ld16(tmem_o + c0, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st16(tmem_o + lane_base + c0, r);
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * scale);
+            tmem_st16(tmem_o + c0, r);
           }
           tmem_wait_st();
         }
       }
+      if (grow) {
+        l *= alpha;
+        m_ref = m_new;
+      }
+      const float mc = m_ref * c;
       float sum = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c0 = 0; c0 < kBlockN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_s + lane_base + c0, r);
-        tmem_wait_ld();
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = (c0 + i < valid) ? exp2f(fmaf(__uint_as_float(r[i]), c, -mc)) : 0.f;
-          const float e1 = (c0 + i + 1 < valid) ? exp2f(fmaf(__uint_as_float(r[i + 1]), c, -mc)) : 0.f;
+          const float e0 = (c0 + i < valid) ? exp2f(fmaf(__uint_as_float(sr[c0 + i]), c, -mc)) : 0.f;
+          const float e1 = (c0 + i + 1 < valid) ? exp2f(fmaf(__uint_as_float(sr[c0 + i + 1]), c, -mc)) : 0.f;
           sum += e0 + e1;
           if constexpr (BF16) {
             __nv_bfloat162 v2 = __floats2bfloat162_rn(e0, e1);
@@ -256,8 +271,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             packed[i / 2] = *reinterpret_cast<uint32_t*>(&v2);
           }
         }
-        // Keys c0..c0+31 of this row: chunk c0/64, 16-byte units u..u+3
-        // at the 128-byte-swizzled positions of row `row`.
+        // Keys c0..c0+31 of this row: chunk c0/64, 16-byte units at the
+        // 128-byte-swizzled positions of row `row`.
         uint8_t* chunk = sp + (c0 >> 6) * (kBlockM * 128) + (row >> 3) * 1024 + (row & 7) * 128;
         const int u0 = (c0 & 63) >> 3;
 #pragma unroll
@@ -267,25 +282,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
         }
       }
-      l = l * alpha + sum;
-      m = m_new;
+      l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[sb]);
-        mbar_arrive(p_ready);
-      }
+      if (lane == 0) mbar_arrive(&p_ready[t]);
     }
-    if (ok && warp_wait(pv_done, (nblocks - 1) & 1, abort_flag, status)) {
+    if (ok && warp_wait(&pv_done[t], (nblocks - 1) & 1, abort_flag, status)) {
       tc_fence_after();
-      const int qrow = q0 + row;
+      const int qrow = q0 + t * kBlockM + row;
       const float inv = 1.f / l;
       T* out = static_cast<T*>(p.out) + (static_cast<long long>(b) * p.lq + qrow) * p.out_ld + h * D;
-#pragma unroll 1
+#pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(tmem_o + lane_base + c0, r);
+        tmem_ld16(tmem_o + c0, r);
         tmem_wait_ld();
         if (qrow < p.lq) {
           uint32_t packed[8];
@@ -326,7 +337,7 @@ int launch_attn(cudaStream_t stream, const CUtensorMap& qm, const CUtensorMap& k
   const int rc = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), Cfg::kSmemBytes, &configured,
                                        "attention smem attribute");
   if (rc != LDB_OK) return rc;
-  dim3 grid((p.lq + kBlockM - 1) / kBlockM, p.heads, p.batch);
+  dim3 grid((p.lq + 2 * kBlockM - 1) / (2 * kBlockM), p.heads, p.batch);
   kernel<<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(qm, km, vm, p, device_status_ptr());
   count_launch();
   return check_cuda(cudaGetLastError(), "attention launch");

@@ -4,8 +4,8 @@
     python -m lesiondiffusion_mlx_b200.kernel_cases [conv|attention|norm|all] [--case NAME] [--iters N]
 
 Each case runs on seeded random inputs and prints one JSON line per case with
-the CUDA-event time per launch and the achieved TFLOP/s or GB/s of its
-algorithmic work.  Conv cases are the distinct 3x3x3 / strided / folded-up
+the CUDA-event time per launch (back-to-back launches replayed from a CUDA
+graph, L2 warm) and the achieved TFLOP/s or GB/s of its algorithmic work.  Conv cases are the distinct 3x3x3 / strided / folded-up
 layer shapes of the config-3 UNet (1 x 32 x 40 x 40 latent) plus BASELINE
 config 1 (the FP32 conv op); attention cases are BASELINE config 2.
 """
@@ -48,23 +48,25 @@ ATTN_CASES = {
 
 
 def _time(fn, iters: int) -> float:
-    """Mean milliseconds per call (CUDA events), after 3 warm-up calls; a 256 MB
-    L2 flush precedes every timed call."""
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    """Mean milliseconds per call: ``iters`` back-to-back calls captured in one
+    CUDA graph and timed with CUDA events (no host launch overhead inside the
+    timed region; L2 is warm across calls)."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
-    total = 0.0
-    for _ in range(iters):
-        flush.zero_()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        fn()
-        e.record()
-        torch.cuda.synchronize()
-        total += s.elapsed_time(e)
-    return total / iters
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(iters):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
 
 
 def conv_case(name: str, iters: int) -> dict:
