@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_begin();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -338,9 +339,8 @@ int launch_attn(cudaStream_t stream, const CUtensorMap& qm, const CUtensorMap& k
                                        "attention smem attribute");
   if (rc != LDB_OK) return rc;
   dim3 grid((p.lq + 2 * kBlockM - 1) / (2 * kBlockM), p.heads, p.batch);
-  kernel<<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(qm, km, vm, p, device_status_ptr());
-  count_launch();
-  return check_cuda(cudaGetLastError(), "attention launch");
+  return launch_kernel(kernel, grid, dim3(kAttnThreads), Cfg::kSmemBytes, stream, "attention launch", qm, km, vm, p,
+                       device_status_ptr());
 }
 
 }  // namespace

@@ -105,6 +105,22 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+// ---------------------------------------------------------------- PDL
+
+// Programmatic dependent launch.  Every kernel of the library is launched
+// with programmatic stream serialization, so it may become resident while the
+// previous kernel of the stream drains.  pdl_wait() blocks until that kernel
+// has completed and its writes are visible: each kernel calls it (after its
+// own shared-memory / TMEM setup) before touching global memory.
+// pdl_trigger() lets the next kernel be scheduled; it is issued right after
+// the wait, so at most two kernels of a stream overlap.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_begin() {
+  pdl_wait();
+  pdl_trigger();
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

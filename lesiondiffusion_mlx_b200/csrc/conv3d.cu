@@ -420,6 +420,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_begin();
 
   const uint32_t a_box_bytes = static_cast<uint32_t>(KC * 2 * p.bw * p.bh * p.bd);
   const uint32_t tx_bytes = Cfg::kPlanes * (a_box_bytes + static_cast<uint32_t>(Cfg::kBBytesRaw));
@@ -585,6 +586,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // of one row of one output tile.
 template <int BN>
 __global__ void conv_reduce_kernel(const ConvParams p) {
+  pdl_begin();
   const int out_tiles = p.num_tiles / p.k_splits;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(out_tiles) * kTileM * (BN / 4);
@@ -650,16 +652,14 @@ int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wm
                                          "conv smem attribute");
     if (rc != LDB_OK) return rc;
   }
-  kernel<<<grid, kConvThreads, smem, stream>>>(maps, wmap, p, device_status_ptr());
-  count_launch();
-  int rc = check_cuda(cudaGetLastError(), "conv3d launch");
+  int rc = launch_kernel(kernel, dim3(grid), dim3(kConvThreads), smem, stream, "conv3d launch", maps, wmap, p,
+                         device_status_ptr());
   if (rc != LDB_OK) return rc;
   if (p.k_splits > 1) {
     const long long total = static_cast<long long>(p.num_tiles / p.k_splits) * kTileM * (BN / 4);
     const int threads = 256;
-    conv_reduce_kernel<BN><<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(p);
-    count_launch();
-    rc = check_cuda(cudaGetLastError(), "conv3d split-K reduce launch");
+    rc = launch_kernel(conv_reduce_kernel<BN>, dim3(static_cast<unsigned>((total + threads - 1) / threads)),
+                       dim3(threads), 0, stream, "conv3d split-K reduce launch", p);
   }
   return rc;
 }

@@ -18,6 +18,7 @@ namespace {
 // the reference's operation order; out is f16 or f32 (B, C).
 __global__ void timestep_embedding_kernel(const int* table, const int* step, int batch, int channels, void* out,
                                           int out_f32) {
+  pdl_begin();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int half = channels / 2;
   if (idx >= batch * half) return;
@@ -52,6 +53,7 @@ constexpr int kDenseMaxRows = 16;
 __global__ void dense_small_kernel(const __half* x, int x_ld, const __half* w, const float* bias, void* out,
                                    int out_ld, int rows, int n_out, int k, int in_silu, int out_silu, int out_f32,
                                    int round_f16) {
+  pdl_begin();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n_out) return;
@@ -140,6 +142,7 @@ struct StepArgs {
 };
 
 __global__ void sampler_step_kernel(StepArgs a) {
+  pdl_begin();
   const long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (v >= a.voxels) return;
   const int C = a.channels;
@@ -222,6 +225,7 @@ __device__ __forceinline__ float vq_norm(float a, float b, float c, float d) {
 template <typename T>
 __global__ void vq_nearest4_kernel(const T* z, int z_ld, long long positions, const T* codebook, int entries,
                                    int* indices, T* quantized, int out_ld) {
+  pdl_begin();
   constexpr int kTile = 1024;
   __shared__ float4 cb[kTile];
   __shared__ float cbn[kTile];
@@ -289,6 +293,7 @@ __global__ void vq_nearest4_kernel(const T* z, int z_ld, long long positions, co
 __global__ void resize_nearest_kernel(const uint8_t* x, int in_d, int in_h, int in_w, uint8_t* out, int od, int oh,
                                       int ow, int batch, int row_bytes, int x_row_stride, int out_row_stride,
                                       float rd, float rh, float rw) {
+  pdl_begin();
   const int groups = row_bytes / 8;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * od * oh * ow * groups;
@@ -317,6 +322,7 @@ __global__ void resize_nearest_kernel(const uint8_t* x, int in_d, int in_h, int 
 // clipping (mlx_pipeline.py:72-96, inverse=True); input f16 or f32 with a
 // channel stride (channel 0 is mapped), output dense f32.
 __global__ void hu_map_kernel(const void* x, int x_f32, int x_ld, long long n, float* out) {
+  pdl_begin();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float a = x_f32 ? static_cast<const float*>(x)[i * x_ld] : __half2float(static_cast<const __half*>(x)[i * x_ld]);
@@ -333,7 +339,10 @@ __global__ void hu_map_kernel(const void* x, int x_f32, int x_ld, long long n, f
   out[i] = r;
 }
 
-__global__ void step_advance_kernel(int* step) { *step += 1; }
+__global__ void step_advance_kernel(int* step) {
+  pdl_begin();
+  *step += 1;
+}
 
 }  // namespace
 }  // namespace ldb
@@ -346,10 +355,8 @@ int ldb_timestep_embedding(cudaStream_t stream, const int* timesteps, const int*
   if (!timesteps || !out) return fail(LDB_ERR_INVALID, "timestep_embedding: null pointer");
   if (batch <= 0 || channels <= 0 || channels % 2) return fail(LDB_ERR_SHAPE, "channels must be even and positive");
   const int n = batch * (channels / 2);
-  timestep_embedding_kernel<<<(n + 255) / 256, 256, 0, stream>>>(timesteps, step, batch, channels, out,
-                                                                  out_dtype == LDB_F32);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "timestep_embedding launch");
+  return launch_kernel(timestep_embedding_kernel, dim3((n + 255) / 256), dim3(256), 0, stream,
+                       "timestep_embedding launch", timesteps, step, batch, channels, out, int(out_dtype == LDB_F32));
 }
 
 int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w, const float* bias, void* out,
@@ -361,11 +368,9 @@ int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w,
   if (n_out <= 0) return fail(LDB_ERR_SHAPE, "n_out must be positive");
   const int threads = 256;
   const int blocks = (n_out * 32 + threads - 1) / threads;
-  dense_small_kernel<<<blocks, threads, 0, stream>>>(static_cast<const __half*>(x), x_ld,
-                                                     static_cast<const __half*>(w), bias, out, out_ld, rows, n_out,
-                                                     k, in_silu, out_silu, out_dtype == LDB_F32, round_f16);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "dense_small launch");
+  return launch_kernel(dense_small_kernel, dim3(blocks), dim3(threads), 0, stream, "dense_small launch",
+                       static_cast<const __half*>(x), x_ld, static_cast<const __half*>(w), bias, out, out_ld, rows,
+                       n_out, k, in_silu, out_silu, int(out_dtype == LDB_F32), round_f16);
 }
 
 int ldb_sampler_step(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_ld,
@@ -403,9 +408,8 @@ int ldb_sampler_step(cudaStream_t stream, int kind, float* x, float* prev, const
   a.channels = channels;
   a.kind = kind;
   const int threads = 256;
-  sampler_step_kernel<<<static_cast<unsigned>((a.voxels + threads - 1) / threads), threads, 0, stream>>>(a);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "sampler_step launch");
+  return launch_kernel(sampler_step_kernel, dim3(static_cast<unsigned>((a.voxels + threads - 1) / threads)),
+                       dim3(threads), 0, stream, "sampler_step launch", a);
 }
 
 int ldb_vq_nearest4(cudaStream_t stream, const void* z, int z_ld, long long positions, const void* codebook,
@@ -416,19 +420,15 @@ int ldb_vq_nearest4(cudaStream_t stream, const void* z, int z_ld, long long posi
   if (z_ld < 4 || (quantized && out_ld < 4)) return fail(LDB_ERR_SHAPE, "strides must cover 4 channels");
   const int threads = 128;
   const unsigned blocks = static_cast<unsigned>((positions + threads - 1) / threads);
-  if (dtype == LDB_F32) {
-    vq_nearest4_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float*>(z), z_ld, positions,
-                                                              static_cast<const float*>(codebook), entries, indices,
-                                                              static_cast<float*>(quantized), out_ld);
-  } else if (dtype == LDB_F16) {
-    vq_nearest4_kernel<__half><<<blocks, threads, 0, stream>>>(static_cast<const __half*>(z), z_ld, positions,
-                                                               static_cast<const __half*>(codebook), entries,
-                                                               indices, static_cast<__half*>(quantized), out_ld);
-  } else {
-    return fail(LDB_ERR_INVALID, "vq_nearest4: dtype must be f16 or f32");
-  }
-  count_launch();
-  return check_cuda(cudaGetLastError(), "vq_nearest4 launch");
+  if (dtype == LDB_F32)
+    return launch_kernel(vq_nearest4_kernel<float>, dim3(blocks), dim3(threads), 0, stream, "vq_nearest4 launch",
+                         static_cast<const float*>(z), z_ld, positions, static_cast<const float*>(codebook), entries,
+                         indices, static_cast<float*>(quantized), out_ld);
+  if (dtype == LDB_F16)
+    return launch_kernel(vq_nearest4_kernel<__half>, dim3(blocks), dim3(threads), 0, stream, "vq_nearest4 launch",
+                         static_cast<const __half*>(z), z_ld, positions, static_cast<const __half*>(codebook),
+                         entries, indices, static_cast<__half*>(quantized), out_ld);
+  return fail(LDB_ERR_INVALID, "vq_nearest4: dtype must be f16 or f32");
 }
 
 int ldb_resize_nearest(cudaStream_t stream, const void* x, int batch, int in_d, int in_h, int in_w, int row_bytes,
@@ -441,30 +441,26 @@ int ldb_resize_nearest(cudaStream_t stream, const void* x, int batch, int in_d, 
     return fail(LDB_ERR_SHAPE, "resize_nearest: extents must be positive");
   const long long total = static_cast<long long>(batch) * out_d * out_h * out_w * (row_bytes / 8);
   const int threads = 256;
-  resize_nearest_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
-      static_cast<const uint8_t*>(x), in_d, in_h, in_w, static_cast<uint8_t*>(out), out_d, out_h, out_w, batch,
-      row_bytes, x_row_stride, out_row_stride, static_cast<float>(static_cast<double>(in_d) / out_d),
-      static_cast<float>(static_cast<double>(in_h) / out_h), static_cast<float>(static_cast<double>(in_w) / out_w));
-  count_launch();
-  return check_cuda(cudaGetLastError(), "resize_nearest launch");
+  return launch_kernel(
+      resize_nearest_kernel, dim3(static_cast<unsigned>((total + threads - 1) / threads)), dim3(threads), 0, stream,
+      "resize_nearest launch", static_cast<const uint8_t*>(x), in_d, in_h, in_w, static_cast<uint8_t*>(out), out_d,
+      out_h, out_w, batch, row_bytes, x_row_stride, out_row_stride,
+      static_cast<float>(static_cast<double>(in_d) / out_d), static_cast<float>(static_cast<double>(in_h) / out_h),
+      static_cast<float>(static_cast<double>(in_w) / out_w));
 }
 
 int ldb_hu_map(cudaStream_t stream, const void* x, int dtype, int x_ld, long long n, float* out) {
   using namespace ldb;
   if (!x || !out || n <= 0) return fail(LDB_ERR_INVALID, "hu_map: bad arguments");
   const int threads = 256;
-  hu_map_kernel<<<static_cast<unsigned>((n + threads - 1) / threads), threads, 0, stream>>>(x, dtype == LDB_F32,
-                                                                                          x_ld, n, out);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "hu_map launch");
+  return launch_kernel(hu_map_kernel, dim3(static_cast<unsigned>((n + threads - 1) / threads)), dim3(threads), 0,
+                       stream, "hu_map launch", x, int(dtype == LDB_F32), x_ld, n, out);
 }
 
 int ldb_step_advance(cudaStream_t stream, int* step) {
   using namespace ldb;
   if (!step) return fail(LDB_ERR_INVALID, "step pointer is null");
-  step_advance_kernel<<<1, 1, 0, stream>>>(step);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "step_advance launch");
+  return launch_kernel(step_advance_kernel, dim3(1), dim3(1), 0, stream, "step_advance launch", step);
 }
 
 }  // extern "C"

@@ -1,5 +1,7 @@
 #include "host_common.h"
 
+#include <cstdlib>
+
 #include <atomic>
 #include <mutex>
 #include <vector>
@@ -69,6 +71,14 @@ int sm_count() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("LDB_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return enabled;
 }
 
 void count_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }

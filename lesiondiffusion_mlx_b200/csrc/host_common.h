@@ -32,6 +32,30 @@ unsigned int* device_status_ptr();
 // Count one kernel launch issued by the library (see ldb_launch_count).
 void count_launch(int n = 1);
 
+// Whether kernels are launched with programmatic stream serialization
+// (default on; LDB_PDL=0 in the environment turns it off).
+bool pdl_enabled();
+
+// Launch `kernel` (every library kernel starts with pdl_begin()) with
+// programmatic stream serialization, count it, and map a launch failure to
+// LDB_ERR_CUDA with `what` in the message.
+template <typename... Params, typename... Args>
+int launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                  const char* what, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  count_launch();
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...), what);
+}
+
 // Raise a kernel's dynamic shared-memory limit once per device (the
 // attribute is per device; setting it again inside a graph capture is
 // avoided).  `flags` is the caller's per-kernel bitset of configured devices.

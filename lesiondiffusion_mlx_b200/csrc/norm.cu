@@ -66,6 +66,7 @@ __device__ __forceinline__ void load8(const Src2& s, long long voxel, int c, flo
 // item.  Block (chunk, b); each thread owns 8 consecutive channels of one
 // voxel row and strides over rows.  partials[b][chunk][c] = (S1, S2).
 __global__ void gn_partial_kernel(Src2 s, int voxels, int chunk_voxels, float2* partials, int nchunks) {
+  pdl_begin();
   const int c_total = s.c1 + s.c2;
   const int vecs = c_total / 8;
   const int b = blockIdx.y;
@@ -124,6 +125,7 @@ __global__ void gn_partial_kernel(Src2 s, int voxels, int chunk_voxels, float2* 
 // shared memory.
 __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, int nchunks, int groups,
                                    const float* gamma, const float* beta, float eps, float* affine) {
+  pdl_begin();
   const int c_total = s.c1 + s.c2;
   const int cpg = c_total / groups;
   const int b = blockIdx.x / groups;
@@ -218,6 +220,7 @@ __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, i
 // written as zeros.  One thread per 8 channels of one voxel.
 __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_batch, const float* affine, int silu,
                                int split, int cpad, __half* out, int out_ld) {
+  pdl_begin();
   const int c_total = s.c1 + s.c2;
   const int vecs = cpad / 8;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -268,6 +271,7 @@ __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_ba
 // FP32 statistics, one rounding.  One warp per row; C <= 1024, C % 8 == 0.
 __global__ void layer_norm_kernel(const __half* x, int x_ld, const float* gamma, const float* beta, float eps,
                                   __half* out, int out_ld, int rows, int C) {
+  pdl_begin();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -431,14 +435,11 @@ int ldb_group_norm_affine(cudaStream_t stream, const void* x1, int c1, int ld1, 
   }
   const int chunk_voxels = (voxels + nchunks - 1) / nchunks;
   float2* partials = static_cast<float2*>(workspace);
-  gn_partial_kernel<<<dim3(nchunks, batch), threads, smem, stream>>>(s, voxels, chunk_voxels, partials, nchunks);
-  count_launch();
-  rc = check_cuda(cudaGetLastError(), "gn_partial launch");
+  rc = launch_kernel(gn_partial_kernel, dim3(nchunks, batch), dim3(threads), smem, stream, "gn_partial launch", s,
+                     voxels, chunk_voxels, partials, nchunks);
   if (rc != LDB_OK) return rc;
-  gn_finalize_kernel<<<batch * groups, 256, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
-                                                         affine);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "gn_finalize launch");
+  return launch_kernel(gn_finalize_kernel, dim3(batch * groups), dim3(256), 0, stream, "gn_finalize launch", s,
+                       voxels, static_cast<const float2*>(partials), nchunks, groups, gamma, beta, eps, affine);
 }
 
 int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2, int ld2,
@@ -456,11 +457,9 @@ int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, cons
   const long long total = static_cast<long long>(batch) * voxels * (cpad / 8);
   if (total <= 0) return fail(LDB_ERR_SHAPE, "empty input");
   const int threads = 256;
-  prepare_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
-      s, static_cast<long long>(batch) * voxels, voxels, affine, silu, split, cpad, static_cast<__half*>(out),
-      out_ld);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "prepare launch");
+  return launch_kernel(prepare_kernel, dim3(static_cast<unsigned>((total + threads - 1) / threads)), dim3(threads),
+                       0, stream, "prepare launch", s, static_cast<long long>(batch) * voxels, voxels, affine, silu,
+                       split, cpad, static_cast<__half*>(out), out_ld);
 }
 
 int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,
@@ -472,10 +471,9 @@ int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* ga
   if (rows <= 0) return fail(LDB_ERR_SHAPE, "rows must be positive");
   const int threads = 256;
   const long long blocks = (static_cast<long long>(rows) * 32 + threads - 1) / threads;
-  layer_norm_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-      static_cast<const __half*>(x), x_ld, gamma, beta, eps, static_cast<__half*>(out), out_ld, rows, channels);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "layer_norm launch");
+  return launch_kernel(layer_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, stream,
+                       "layer_norm launch", static_cast<const __half*>(x), x_ld, gamma, beta, eps,
+                       static_cast<__half*>(out), out_ld, rows, channels);
 }
 
 // GroupNorm affine without any allocation: the same statistics as
