@@ -106,6 +106,20 @@ typedef struct {
 /* Workspace bytes ldb_conv3d_fwd needs (split-K partial tiles; 0 if none). */
 LDB_API int ldb_conv3d_workspace_size(const ldb_conv_desc* desc, size_t* bytes);
 
+/* ldb_conv3d_fwd that also adds, per (batch, output channel), the sum and the
+ * sum of squares of the output values as stored into `stats` (FP64,
+ * [batch][out_channels][2]; zero it before the first producer call).  These
+ * are the GroupNorm statistics of the output, so the layer that normalizes
+ * it (ldb_group_norm_affine_from_stats) needs no statistics pass of its own.  The
+ * reference computes them in the GroupNorm call that follows the conv
+ * (medmlx-core group_norm_affine at lesiondiffusion_mlx/mlx_model.py:328-335);
+ * summation order follows the GPU schedule, so the last bits can differ
+ * between runs. */
+LDB_API int ldb_conv3d_fwd_gn_stats(ldb_stream_t stream, const ldb_conv_desc* desc, const void* x,
+                                    const void* w_packed, const float* bias, const float* shift,
+                                    const void* residual, void* out, double* stats, void* workspace,
+                                    size_t workspace_bytes);
+
 /* Packed-weight geometry for `desc`: rows per parity (Cout padded to the
  * kernel's column tile) and K elements per row (taps * Cin_pad [* 2]). */
 LDB_API int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_parity, int* k_total);
@@ -151,6 +165,17 @@ LDB_API int ldb_group_norm_affine_noalloc(ldb_stream_t stream, const void* x1, i
 LDB_API int ldb_prepare_input(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
                               int ld2, int dtype, int batch, int voxels, const float* affine, int silu, int split,
                               void* out, int out_ld);
+
+/* GroupNorm affine (scale, offset per batch and channel, as
+ * ldb_group_norm_affine) from producer statistics instead of a pass over the
+ * tensor: `stats1` / `stats2` are the FP64 [batch][channels][2] sums and sums
+ * of squares of the two channel blocks [x1 | x2] (x2 may be absent, c2 = 0),
+ * as ldb_conv3d_fwd_gn_stats accumulates them; `voxels` per batch item.
+ * Replaces the statistics half of medmlx-core's group_norm_affine
+ * (lesiondiffusion_mlx/mlx_model.py:328-335). */
+LDB_API int ldb_group_norm_affine_from_stats(ldb_stream_t stream, const double* stats1, int c1,
+                                             const double* stats2, int c2, int batch, int voxels, int groups,
+                                             const float* gamma, const float* beta, float eps, float* affine);
 
 /* LayerNorm over the last axis of f16 rows (mlx_model.py:360-367). */
 LDB_API int ldb_layer_norm(ldb_stream_t stream, const void* x, int x_ld, const float* gamma, const float* beta,

@@ -63,10 +63,12 @@ SIGNATURES: dict[str, list] = {
     "ldb_conv3d_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_SZ)],
     "ldb_conv3d_weight_rows": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_I), ctypes.POINTER(_I)],
     "ldb_conv3d_fwd": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _SZ],
+    "ldb_conv3d_fwd_gn_stats": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _P, _SZ],
     "ldb_group_norm_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
     "ldb_group_norm_affine": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _SZ],
     "ldb_group_norm_affine_noalloc": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P],
     "ldb_prepare_input": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I],
+    "ldb_group_norm_affine_from_stats": [_P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _F, _P],
     "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
     "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],
     "ldb_step_advance": [_P, _P],

@@ -187,6 +187,7 @@ def conv3d_ndhwc(
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype | None = None,
     in_channels: int | None = None,
+    stats: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
@@ -195,6 +196,9 @@ def conv3d_ndhwc(
     ``residual`` has the output's dtype and shape.  The output is NDHWC with
     ``O`` channels; a new output has its channel stride padded to 8 so it can
     feed the next convolution.  Stride applies only to ``kind == "conv"``.
+    With ``stats`` (float64 ``(B, O, 2)``, zero on entry) the kernel also adds
+    each channel's sum and sum of squares of the stored output: the GroupNorm
+    statistics that ``ops.group_norm_affine_from_stats`` consumes.
     """
     if x.device.type != "cuda":
         raise ValueError("conv3d_ndhwc needs CUDA tensors")
@@ -238,9 +242,19 @@ def conv3d_ndhwc(
     stream = torch.cuda.current_stream(x.device).cuda_stream
     taps = {MODE_POINTWISE: 1, MODE_UP2: 8}.get(mode, 27)
     flops = 2.0 * batch * grid[0] * grid[1] * grid[2] * cout * taps * cin
+    if stats is not None and (stats.dtype != torch.float64 or tuple(stats.shape) != (batch, cout, 2)
+                              or not stats.is_contiguous()):
+        raise ValueError(f"stats must be a contiguous float64 {(batch, cout, 2)} tensor")
     with instrument.maybe_time("conv3d", flops):
-        _lib.call(
-            "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
-            _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,
-        )
+        if stats is None:
+            _lib.call(
+                "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
+                _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,
+            )
+        else:
+            _lib.call(
+                "ldb_conv3d_fwd_gn_stats", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(),
+                _ptr(bias), _ptr(shift), _ptr(residual), out.data_ptr(), stats.data_ptr(), _ptr(workspace),
+                ws_bytes.value,
+            )
     return out

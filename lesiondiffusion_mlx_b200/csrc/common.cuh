@@ -121,6 +121,12 @@ __device__ __forceinline__ void pdl_begin() {
   pdl_trigger();
 }
 
+// Fire-and-forget FP64 add to global memory (no value returned, so the
+// thread does not wait for the L2 round trip).
+__device__ __forceinline__ void red_add_f64(double* addr, double v) {
+  asm volatile("red.global.add.f64 [%0], %1;" ::"l"(addr), "d"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

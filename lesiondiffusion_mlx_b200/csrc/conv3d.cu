@@ -83,7 +83,8 @@ __device__ __forceinline__ long long row_voxel(const ConvParams& p, const TileCo
 }
 
 // Apply the epilogue to `n` consecutive output channels starting at `col`
-// of one voxel and store them.  `v` holds the f32 GEMM sums.
+// of one voxel and store them.  `v` holds the f32 GEMM sums on entry and the
+// values as stored (after the output rounding) on return.
 template <int N>
 __device__ __forceinline__ void store_outputs(const ConvParams& p, int b, long long voxel, int col, float (&v)[N]) {
   const bool full = (col + N <= p.cout);
@@ -152,13 +153,21 @@ __device__ __forceinline__ void store_outputs(const ConvParams& p, int b, long l
         uint4 raw;
         __half2* h2 = reinterpret_cast<__half2*>(&raw);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) h2[q] = __floats2half2_rn(v[j + 2 * q], v[j + 2 * q + 1]);
+        for (int q = 0; q < 4; ++q) {
+          h2[q] = __floats2half2_rn(v[j + 2 * q], v[j + 2 * q + 1]);
+          const float2 f = __half22float2(h2[q]);
+          v[j + 2 * q] = f.x;
+          v[j + 2 * q + 1] = f.y;
+        }
         *reinterpret_cast<uint4*>(o + j) = raw;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < N; ++j)
-        if (col + j < p.cout) o[j] = __float2half_rn(v[j]);
+      for (int j = 0; j < N; ++j) {
+        const __half h = __float2half_rn(v[j]);
+        v[j] = __half2float(h);
+        if (col + j < p.cout) o[j] = h;
+      }
     }
   }
 }
@@ -176,7 +185,9 @@ struct ConvCfg {
   // Epilogue staging: 2 output + 2 residual buffers of 128 rows x 128 bytes.
   static constexpr int kEpiBufBytes = kTileM * 128;
   static constexpr int kEpiBytes = 4 * kEpiBufBytes;
-  static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048) / kStageBytes;
+  // Per-CTA GroupNorm statistics accumulator: [BN][2] FP32 shifted sums.
+  static constexpr int kStatsBytes = BN * 8;
+  static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048 - kStatsBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * kPlanes;
   static constexpr int kTmemColsRaw = 2 * kAccCols;
@@ -190,7 +201,7 @@ struct ConvCfg {
   // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, res_full[2]
   static constexpr int kBarrierBytes = (2 * kStages + 7) * 8;
   static constexpr int kSmemBytes =
-      kStages * kStageBytes + kEpiBytes + 1024 /*align slack*/ + kBarrierBytes + 64 + BN * 4;
+      kStages * kStageBytes + kEpiBytes + 1024 /*align slack*/ + kBarrierBytes + 64 + BN * 4 + kStatsBytes;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -200,6 +211,11 @@ struct EpiState {
   uint8_t* epi;          // out staging [2] then residual staging [2], 128 rows x 128 B each
   uint64_t* res_full;    // [2]
   float* bsum;           // [BN]
+  uint32_t* vmask;       // [2][4] valid-row bits of the current tile (double-buffered by tile)
+  float* sacc;           // [BN][2] sums of (x - bsum) and (x - bsum)^2 over the current run of tiles
+  int key_b = -1;        // (batch, column tile) of the run: tiles of one run share bsum
+  int key_nt = -1;
+  int run_rows = 0;      // valid rows (voxels) accumulated in the run
   volatile int* abort_flag;
   unsigned int* status;
   int quarter, row;
@@ -208,7 +224,98 @@ struct EpiState {
   uint32_t rq = 0;               // residual chunks consumed
   uint32_t res_uses0 = 0;        // completed phases of residual buffer 0
   uint32_t res_uses1 = 0;        // ... and of buffer 1
+  uint32_t tiles = 0;            // tiles started (valid-row mask parity)
 };
+
+// GroupNorm statistics of one staged output chunk (the values exactly as
+// stored).  Each thread owns one 4-byte word of the staged rows (two f16 or
+// one f32 column) over its part of the tile's rows, loads 8 rows at a time
+// and sums the valid rows' x - k and (x - k)^2 in FP32, k being the column's
+// bias + shift (constant over a run of tiles, and close to the column mean,
+// so the shifted sums keep the variance from cancelling).  The parts fold
+// into the CTA's accumulator with shared-memory FP32 atomics.
+template <int CC, int kElem>
+__device__ __forceinline__ void chunk_stats(const ConvParams& p, int n0, int c0, const uint8_t* ob,
+                                            const uint32_t* vmask, const float* bsum, float* sacc) {
+  constexpr uint32_t kRowBytes = CC * kElem;
+  constexpr int kThreadsPerRow = kRowBytes / 4;
+  constexpr int kColsPer = 4 / kElem;
+  constexpr int kParts = 128 / kThreadsPerRow;
+  constexpr int kRows = kTileM / kParts;  // 8, 16 or 32
+  const int et = threadIdx.x - 64;
+  const int w = et % kThreadsPerRow;
+  const int part = et / kThreadsPerRow;
+  const int jt = c0 + w * kColsPer;  // first column within the tile
+  if (n0 + jt >= p.cout) return;
+  const int r0 = part * kRows;
+  const uint32_t bits = (vmask[r0 >> 5] >> (r0 & 31)) & (kRows == 32 ? 0xffffffffu : ((1u << kRows) - 1u));
+  if (bits == 0) return;
+  float k[kColsPer], s1[kColsPer], s2[kColsPer];
+#pragma unroll
+  for (int q = 0; q < kColsPer; ++q) {
+    k[q] = bsum[jt + q];
+    s1[q] = s2[q] = 0.f;
+  }
+#pragma unroll 1
+  for (int i0 = 0; i0 < kRows; i0 += 8) {
+    uint32_t words[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      words[u] = *reinterpret_cast<const uint32_t*>(
+          ob + swizzle_offset(static_cast<uint32_t>(r0 + i0 + u) * kRowBytes + w * 4, kRowBytes));
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if ((bits >> (i0 + u)) & 1u) {
+        float x[kColsPer];
+        if constexpr (kElem == 4) {
+          x[0] = __uint_as_float(words[u]);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[u]));
+          x[0] = f.x;
+          x[1] = f.y;
+        }
+#pragma unroll
+        for (int q = 0; q < kColsPer; ++q) {
+          const float d = x[q] - k[q];
+          s1[q] += d;
+          s2[q] = fmaf(d, d, s2[q]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kColsPer; ++q) {
+    if (n0 + jt + q >= p.cout) break;
+    atomicAdd(&sacc[(jt + q) * 2], s1[q]);
+    atomicAdd(&sacc[(jt + q) * 2 + 1], s2[q]);
+  }
+}
+
+// Add the CTA's statistics of the finished run (key_b, key_nt) to the global
+// FP64 totals, one add pair per column: sum = S1 + n k and sum of squares =
+// S2 + 2 k S1 + n k^2 with k the run's bias + shift (still in bsum), then
+// optionally clear the accumulator.  Called by the 128 epilogue threads
+// after a named barrier.
+template <int BN>
+__device__ __forceinline__ void flush_stats(const ConvParams& p, const EpiState& st, bool clear) {
+  for (int j = threadIdx.x - 64; j < BN; j += 128) {
+    if (st.key_b >= 0 && st.run_rows > 0) {
+      const int col = st.key_nt * BN + j;
+      if (col < p.cout) {
+        const double n = st.run_rows;
+        const double k = st.bsum[j];
+        const double s1 = st.sacc[2 * j], s2 = st.sacc[2 * j + 1];
+        double* dst = p.stats + (static_cast<long long>(st.key_b) * p.cout + col) * 2;
+        red_add_f64(dst, s1 + n * k);
+        red_add_f64(dst + 1, s2 + 2.0 * k * s1 + n * k * k);
+      }
+    }
+    if (clear) {
+      st.sacc[2 * j] = 0.f;
+      st.sacc[2 * j + 1] = 0.f;
+    }
+  }
+}
 
 // One output tile: wait for its accumulator, then per chunk of CC columns
 // TMEM -> registers -> (bias + shift) * scale + residual -> GELU -> round ->
@@ -238,6 +345,20 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
   // Never leave early: the four epilogue warps must reach the same sequence
   // of named barriers.  After a timeout the waits below fail fast (the abort
   // flag is set) and the tile is written with whatever TMEM holds.
+  uint32_t* vmask = st.vmask + (st.tiles & 1) * 4;
+  st.tiles += 1;
+  if (!SPLIT && p.stats) {
+    if (c.b != st.key_b || c.nt != st.key_nt) {
+      // a new (batch, column tile): hand the previous run's sums to the totals
+      named_barrier(1, 128);
+      flush_stats<BN>(p, st, true);
+      st.key_b = c.b;
+      st.key_nt = c.nt;
+      st.run_rows = 0;
+    }
+    const unsigned int valid = __ballot_sync(0xffffffffu, row_voxel(p, c, st.row) >= 0);
+    if ((st.row & 31) == 0) vmask[st.quarter] = valid;
+  }
   bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
   tc_fence_after();
   if (!SPLIT) {
@@ -252,6 +373,8 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
     }
   }
   named_barrier(1, 128);
+  if (!SPLIT && p.stats)  // every thread counts the tile's valid rows (the masks are visible after the barrier)
+    st.run_rows += static_cast<int>(__popc(vmask[0]) + __popc(vmask[1]) + __popc(vmask[2]) + __popc(vmask[3]));
   const uint32_t rowoff = static_cast<uint32_t>(st.row) * kRowBytes;
 #pragma unroll 1
   for (int q = 0; q < kChunks; ++q) {
@@ -356,6 +479,9 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
       }
       bulk_commit_group();
     }
+    if constexpr (!SPLIT) {
+      if (p.stats) chunk_stats<CC, kElem>(p, n0, c0, ob, vmask, st.bsum, st.sacc);
+    }
     st.oq += 1;
   }
   return ok;
@@ -377,7 +503,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t* res_full = drain + 1;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* vmask = tmem_slot + 4;                          // [2][4]
   float* bsum = reinterpret_cast<float*>(tmem_slot + 16);  // [BN] bias + shift of the current tile
+  float* sacc = bsum + BN;                                  // [BN][2] GroupNorm statistics
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -549,6 +677,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     st.epi = epi;
     st.res_full = res_full;
     st.bsum = bsum;
+    st.vmask = vmask;
+    st.sacc = sacc;
     st.abort_flag = abort_flag;
     st.status = status;
     st.quarter = warp & 3;
@@ -571,6 +701,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (p.stats && !split && st.key_b >= 0) {
+      named_barrier(1, 128);
+      flush_stats<BN>(p, st, false);
+    }
     if (st.leader) bulk_wait_group_all();  // stores must finish before the CTA releases its shared memory
   }
 
@@ -582,32 +716,118 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
 }
 
-// Sum split-K partial tiles and apply the epilogue: one thread per 4 columns
-// of one row of one output tile.
-template <int BN>
-__global__ void conv_reduce_kernel(const ConvParams p) {
+// Sum split-K partial tiles and apply the epilogue.  Block (slab, row
+// block, out_tile) of 256 threads covers up to 64 columns x kRowLanes x
+// kRowsPer rows of one output tile; thread (cq, rl) owns 4 columns of rows
+// rl + kRowLanes * i and sums their K ranges (all rows' loads of a K range
+// issued together).  With GroupNorm statistics requested, the rows' stored
+// values are summed around the column's bias + shift in FP32 (lanes sharing
+// a column by shuffles, warps by shared atomics) and the block adds one FP64
+// pair per column to the totals.
+template <int BN, int ROWS>
+__global__ void __launch_bounds__(256) conv_reduce_kernel(const ConvParams p) {
   pdl_begin();
+  constexpr int kSlab = BN < 64 ? BN : 64;
+  constexpr int kQ = kSlab / 4;
+  constexpr int kRowLanes = 256 / kQ;
+  constexpr int kRowsPer = kTileM / kRowLanes < ROWS ? kTileM / kRowLanes : ROWS;
+  __shared__ float red[2][kSlab];
+  __shared__ int valid_rows;
   const int out_tiles = p.num_tiles / p.k_splits;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(out_tiles) * kTileM * (BN / 4);
-  if (idx >= total) return;
-  const int q = static_cast<int>(idx % (BN / 4));
-  const int row = static_cast<int>((idx / (BN / 4)) % kTileM);
-  const int ot = static_cast<int>(idx / (static_cast<long long>(BN / 4) * kTileM));
+  const int ot = blockIdx.z;
+  const int cq = threadIdx.x % kQ;
+  const int rl = threadIdx.x / kQ;
+  const int row0 = blockIdx.y * kRowLanes * kRowsPer + rl;
+  const int col_t = blockIdx.x * kSlab + cq * 4;  // column within the tile
   const TileCoord c = decode_tile(p, ot * p.k_splits);
-  const long long voxel = row_voxel(p, c, row);
-  const int col = c.nt * BN + q * 4;
-  if (voxel < 0 || col >= p.cout) return;
-  float v[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < p.k_splits; ++s) {
-    const float4 f = *reinterpret_cast<const float4*>(
-        p.partials + ((static_cast<long long>(s) * out_tiles + ot) * kTileM + row) * BN + q * 4);
-    v[0] += f.x;
-    v[1] += f.y;
-    v[2] += f.z;
-    v[3] += f.w;
+  const int col = c.nt * BN + col_t;
+  const bool stats = p.stats != nullptr;
+  if (stats) {
+    for (int i = threadIdx.x; i < 2 * kSlab; i += blockDim.x) red[i / kSlab][i % kSlab] = 0.f;
+    if (threadIdx.x == 0) valid_rows = 0;
+    __syncthreads();
   }
-  store_outputs<4>(p, c.b, voxel, col, v);
+  float v[kRowsPer][4];
+#pragma unroll
+  for (int i = 0; i < kRowsPer; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[i][j] = 0.f;
+  if (col < p.cout) {
+    const float* src = p.partials + (static_cast<long long>(ot) * kTileM + row0) * BN + col_t;
+    const long long split_stride = static_cast<long long>(out_tiles) * kTileM * BN;
+#pragma unroll 2
+    for (int s = 0; s < p.k_splits; ++s) {
+      float4 f[kRowsPer];
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i)
+        f[i] = *reinterpret_cast<const float4*>(src + s * split_stride + static_cast<long long>(i) * kRowLanes * BN);
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i) {
+        v[i][0] += f[i].x;
+        v[i][1] += f[i].y;
+        v[i][2] += f[i].z;
+        v[i][3] += f[i].w;
+      }
+    }
+  }
+  bool live[kRowsPer];
+  int nvalid = 0;
+#pragma unroll
+  for (int i = 0; i < kRowsPer; ++i) {
+    const long long voxel = row_voxel(p, c, row0 + i * kRowLanes);
+    live[i] = voxel >= 0 && col < p.cout;
+    nvalid += voxel >= 0;
+    if (live[i]) store_outputs<4>(p, c.b, voxel, col, v[i]);
+  }
+  if (!stats) return;
+  float k[4], d1[4], d2[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int cj = col + j;
+    k[j] = 0.f;
+    if (cj < p.cout) {
+      if (p.bias) k[j] = p.bias[cj];
+      if (p.shift) k[j] += p.shift[static_cast<long long>(c.b) * p.cout + cj];
+    }
+    d1[j] = d2[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowsPer; ++i) {
+      const float d = live[i] ? v[i][j] - k[j] : 0.f;
+      d1[j] += d;
+      d2[j] = fmaf(d, d, d2[j]);
+    }
+  }
+#pragma unroll
+  for (int o = kQ; o < 32; o <<= 1) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      d1[j] += __shfl_xor_sync(0xffffffffu, d1[j], o);
+      d2[j] += __shfl_xor_sync(0xffffffffu, d2[j], o);
+    }
+  }
+  if ((threadIdx.x & 31) < kQ) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      atomicAdd(&red[0][cq * 4 + j], d1[j]);
+      atomicAdd(&red[1][cq * 4 + j], d2[j]);
+    }
+  }
+  if (cq == 0 && nvalid) atomicAdd(&valid_rows, nvalid);
+  __syncthreads();
+  const int n = valid_rows;
+  for (int j = threadIdx.x; j < kSlab; j += blockDim.x) {
+    const int cc = c.nt * BN + blockIdx.x * kSlab + j;
+    if (cc < p.cout && n > 0) {
+      double kk = 0.0;
+      if (p.bias) kk = p.bias[cc];
+      if (p.shift) kk += p.shift[static_cast<long long>(c.b) * p.cout + cc];
+      kk = static_cast<float>(kk);
+      const double s1 = red[0][j], s2 = red[1][j];
+      double* dst = p.stats + (static_cast<long long>(c.b) * p.cout + cc) * 2;
+      red_add_f64(dst, s1 + n * kk);
+      red_add_f64(dst + 1, s2 + 2.0 * kk * s1 + n * kk * kk);
+    }
+  }
 }
 
 // Brick of at most 128 voxels covering a (d, h, w) grid with the fewest
@@ -656,10 +876,15 @@ int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wm
                          device_status_ptr());
   if (rc != LDB_OK) return rc;
   if (p.k_splits > 1) {
-    const long long total = static_cast<long long>(p.num_tiles / p.k_splits) * kTileM * (BN / 4);
-    const int threads = 256;
-    rc = launch_kernel(conv_reduce_kernel<BN>, dim3(static_cast<unsigned>((total + threads - 1) / threads)),
-                       dim3(threads), 0, stream, "conv3d split-K reduce launch", p);
+    // Many K ranges: one row per thread (more blocks, more loads in flight);
+    // few: four rows per thread (fewer blocks, fewer statistics atomics).
+    constexpr int kSlab = BN < 64 ? BN : 64;
+    constexpr int kRowLanes = 256 / (kSlab / 4);
+    constexpr int kRows4 = kTileM / kRowLanes < 4 ? kTileM / kRowLanes : 4;
+    const bool deep = p.k_splits >= 6;
+    rc = launch_kernel(deep ? conv_reduce_kernel<BN, 1> : conv_reduce_kernel<BN, 4>,
+                       dim3(BN / kSlab, kTileM / (kRowLanes * (deep ? 1 : kRows4)), p.num_tiles / p.k_splits),
+                       dim3(256), 0, stream, "conv3d split-K reduce launch", p);
   }
   return rc;
 }
@@ -789,9 +1014,9 @@ int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_parity, int*
   return LDB_OK;
 }
 
-int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
-                   const float* bias, const float* shift, const void* residual, void* out, void* workspace,
-                   size_t workspace_bytes) {
+static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
+                        const float* bias, const float* shift, const void* residual, void* out, double* stats,
+                        void* workspace, size_t workspace_bytes) {
   using namespace ldb;
   ConvPlan plan;
   int rc = plan_conv(desc, &plan);
@@ -809,6 +1034,7 @@ int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x
   p.shift = shift;
   p.residual = residual;
   p.out = out;
+  p.stats = stats;
   p.partials = static_cast<float*>(workspace);
 
   const int B = desc->batch, D = desc->depth, H = desc->height, W = desc->width;
@@ -918,6 +1144,19 @@ int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x
       return exact ? dispatch_bn<64, true>(plan.bn, stream, maps, wmap, p, plan.grid)
                    : dispatch_bn<64, false>(plan.bn, stream, maps, wmap, p, plan.grid);
   }
+}
+
+int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
+                   const float* bias, const float* shift, const void* residual, void* out, void* workspace,
+                   size_t workspace_bytes) {
+  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, nullptr, workspace, workspace_bytes);
+}
+
+int ldb_conv3d_fwd_gn_stats(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
+                            const float* bias, const float* shift, const void* residual, void* out, double* stats,
+                            void* workspace, size_t workspace_bytes) {
+  if (!stats) return ldb::fail(LDB_ERR_INVALID, "conv3d: stats is null");
+  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, stats, workspace, workspace_bytes);
 }
 
 }  // extern "C"

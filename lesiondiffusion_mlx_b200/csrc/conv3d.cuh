@@ -48,6 +48,9 @@ struct ConvParams {
   float out_scale;
   int act;
   float* partials;
+  // GroupNorm statistics of the stored output (may be null): per (batch,
+  // channel) the FP64 sum and sum of squares, added atomically.
+  double* stats;
   int out_d, out_h, out_w;
 };
 

@@ -267,6 +267,48 @@ __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_ba
   if (split) *reinterpret_cast<uint4*>(o + cpad) = lo_raw;
 }
 
+// GroupNorm affine from producer statistics: per (batch, channel) FP64 sum
+// and sum of squares of each source block, as the convolution epilogue adds
+// them up.  One warp per (group, batch): lanes stride over the group's
+// channels, a shuffle tree gives every lane the totals, and each lane writes
+// (scale, offset) of its channels with the same arithmetic as
+// gn_finalize_kernel (biased variance over the group's channels and voxels).
+__global__ void gn_stats_affine_kernel(const double* st1, int c1, const double* st2, int c2, int voxels,
+                                       int groups, const float* gamma, const float* beta, float eps,
+                                       float* affine) {
+  pdl_begin();
+  const int C = c1 + c2;
+  const int cpg = C / groups;
+  const int b = blockIdx.y;
+  const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (g >= groups) return;
+  double a = 0.0, q = 0.0;
+  for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
+    const double* src = c < c1 ? st1 + (static_cast<long long>(b) * c1 + c) * 2
+                               : st2 + (static_cast<long long>(b) * c2 + (c - c1)) * 2;
+    a += src[0];
+    q += src[1];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  const double inv_n = 1.0 / (static_cast<double>(voxels) * cpg);
+  const double mean = a * inv_n;
+  const double var = fmax(q * inv_n - mean * mean, 0.0);
+  const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
+  for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
+    const float gam = gamma ? gamma[c] : 1.f;
+    const float bet = beta ? beta[c] : 0.f;
+    const float scale = static_cast<float>(static_cast<double>(gam) * rstd);
+    const float offset = static_cast<float>(static_cast<double>(bet) - mean * static_cast<double>(scale));
+    affine[(static_cast<long long>(b) * C + c) * 2] = scale;
+    affine[(static_cast<long long>(b) * C + c) * 2 + 1] = offset;
+  }
+}
+
 // LayerNorm over the last axis of (rows, C) f16 (mlx_model.py:360-367):
 // FP32 statistics, one rounding.  One warp per row; C <= 1024, C % 8 == 0.
 __global__ void layer_norm_kernel(const __half* x, int x_ld, const float* gamma, const float* beta, float eps,
@@ -460,6 +502,20 @@ int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, cons
   return launch_kernel(prepare_kernel, dim3(static_cast<unsigned>((total + threads - 1) / threads)), dim3(threads),
                        0, stream, "prepare launch", s, static_cast<long long>(batch) * voxels, voxels, affine, silu,
                        split, cpad, static_cast<__half*>(out), out_ld);
+}
+
+int ldb_group_norm_affine_from_stats(cudaStream_t stream, const double* stats1, int c1, const double* stats2,
+                                     int c2, int batch, int voxels, int groups, const float* gamma,
+                                     const float* beta, float eps, float* affine) {
+  using namespace ldb;
+  if (!stats1 || !affine || (c2 > 0 && !stats2)) return fail(LDB_ERR_INVALID, "gn affine from stats: null pointer");
+  if (c1 <= 0 || c2 < 0 || batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "extents must be positive");
+  const int C = c1 + c2;
+  if (groups <= 0 || C % groups) return fail(LDB_ERR_SHAPE, "groups %d must divide channels %d", groups, C);
+  const int threads = 256;
+  return launch_kernel(gn_stats_affine_kernel, dim3((groups * 32 + threads - 1) / threads, batch), dim3(threads), 0,
+                       stream, "gn affine from stats launch", stats1, c1, c2 > 0 ? stats2 : stats1, c2, voxels,
+                       groups, gamma, beta, eps, affine);
 }
 
 int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,

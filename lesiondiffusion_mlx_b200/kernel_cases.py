@@ -69,7 +69,7 @@ def _time(fn, iters: int) -> float:
     return s.elapsed_time(e) / iters
 
 
-def conv_case(name: str, iters: int) -> dict:
+def conv_case(name: str, iters: int, stats: bool = False) -> dict:
     d, h, w, cin, cout, kind = CONV_CASES[name]
     g = torch.Generator(device="cuda").manual_seed(0)
     exact = kind == "exact"
@@ -84,12 +84,14 @@ def conv_case(name: str, iters: int) -> dict:
         x = torch.randn((1, d, h, w, cin), generator=g, device="cuda").to(torch.float16)
         packed = pack_upsample_weight(wt.half()) if kind == "up" else pack_weight(wt.half(), stride=2 if kind == "s2" else 1)
     stride = 2 if kind == "s2" else 1
-    fn = lambda: conv3d_ndhwc(x, packed, bias, stride=stride, in_channels=cin)  # noqa: E731
+    st = torch.zeros((1, cout, 2), dtype=torch.float64, device="cuda") if stats else None
+    fn = lambda: conv3d_ndhwc(x, packed, bias, stride=stride, in_channels=cin, stats=st)  # noqa: E731
     ms = _time(fn, iters)
     out_vox = {"s2": ((d + 1) // 2) * ((h + 1) // 2) * ((w + 1) // 2), "up": 8 * d * h * w}.get(kind, d * h * w)
     taps = {"pw": 1, "up": 8}.get(kind, 27)
     flops = 2.0 * out_vox * cout * taps * cin
-    return {"kernel": "conv3d", "case": name, "shape": [d, h, w, cin, cout], "kind": kind, "ms": ms,
+    return {"kernel": "conv3d+stats" if stats else "conv3d", "case": name, "shape": [d, h, w, cin, cout],
+            "kind": kind, "ms": ms,
             "tflops": flops / ms / 1e9, "gflop": flops / 1e9}
 
 
@@ -114,9 +116,14 @@ def norm_case(iters: int) -> list[dict]:
         ms_gn = _time(lambda: ops.group_norm_affine(x, gam, gam, groups=32, eps=1e-5), iters)
         aff = ops.group_norm_affine(x, gam, gam, groups=32, eps=1e-5)
         ms_pr = _time(lambda: ops.prepare_input(x, affine=aff, silu=True), iters)
+        xs = x.double().reshape(1, -1, c)
+        st = torch.stack([xs.sum(1), (xs * xs).sum(1)], dim=-1).contiguous()
+        ms_af = _time(lambda: ops.group_norm_affine_from_stats(st, gam, gam, voxels=d * h * w, groups=32, eps=1e-5),
+                      iters)
         nbytes = x.numel() * 2
         out.append({"kernel": "group_norm_stats", "shape": [d, h, w, c], "ms": ms_gn, "gbs": nbytes / ms_gn / 1e6})
         out.append({"kernel": "prepare", "shape": [d, h, w, c], "ms": ms_pr, "gbs": 2 * nbytes / ms_pr / 1e6})
+        out.append({"kernel": "group_norm_affine_from_stats", "shape": [d, h, w, c], "ms": ms_af})
     return out
 
 
@@ -125,10 +132,11 @@ def main() -> None:
     ap.add_argument("what", nargs="?", default="all", choices=("conv", "attention", "norm", "all"))
     ap.add_argument("--case", default=None)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--stats", action="store_true", help="conv cases also accumulate GroupNorm statistics")
     a = ap.parse_args()
     if a.what in ("conv", "all"):
         for name in ([a.case] if a.case else CONV_CASES):
-            print(json.dumps(conv_case(name, a.iters)), flush=True)
+            print(json.dumps(conv_case(name, a.iters, stats=a.stats)), flush=True)
     if a.what in ("attention", "all"):
         for name in ([a.case] if a.case and a.what == "attention" else ATTN_CASES):
             print(json.dumps(attn_case(name, a.iters)), flush=True)

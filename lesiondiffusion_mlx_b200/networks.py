@@ -109,25 +109,67 @@ def _voxels(x: torch.Tensor) -> tuple[int, int, int]:
     return int(x.shape[1]), int(x.shape[2]), int(x.shape[3])
 
 
+_GN_STATS = "_ldb_gn_stats"  # attribute of a conv output that carries its GroupNorm statistics
+
+
 class _Layers:
     def __init__(self, params: _Params):
         self.p = params
+        # Per-forward float64 arena (zeroed once per forward) that conv outputs
+        # feeding a GroupNorm take their statistics slices from.
+        self._arena: torch.Tensor | None = None
+        self._arena_pos = 0
+        self._stats_channels = sum(int(w.shape[0]) for w in params.raw.values() if w.ndim == 5)
+
+    def _begin_stats(self, batch: int, device: torch.device) -> None:
+        self._arena = torch.zeros(batch * self._stats_channels * 2, dtype=torch.float64, device=device)
+        self._arena_pos = 0
+
+    def _take_stats(self, batch: int, channels: int) -> torch.Tensor | None:
+        n = batch * channels * 2
+        if self._arena is None or self._arena_pos + n > self._arena.numel():
+            return None
+        t = self._arena[self._arena_pos : self._arena_pos + n].view(batch, channels, 2)
+        self._arena_pos += n
+        return t
 
     def conv(self, x: torch.Tensor, key: str, *, stride: int = 1, residual: torch.Tensor | None = None,
-             shift: torch.Tensor | None = None, output_scale: float = 1.0) -> torch.Tensor:
-        """3x3x3 (stride 1/2, or folded up-2x) or pointwise conv of NDHWC f16 x."""
+             shift: torch.Tensor | None = None, output_scale: float = 1.0, stats: bool = False) -> torch.Tensor:
+        """3x3x3 (stride 1/2, or folded up-2x) or pointwise conv of NDHWC f16 x.
+
+        With ``stats`` the output also carries its GroupNorm statistics,
+        accumulated by the conv epilogue, for the GroupNorm that reads it."""
         packed = self.p.conv(key, stride)
-        return conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
-                            output_scale=output_scale)
+        st = self._take_stats(int(x.shape[0]), packed.out_channels) if stats else None
+        out = conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
+                           output_scale=output_scale, stats=st)
+        if st is not None:
+            setattr(out, _GN_STATS, st)
+        return out
+
+    def group_norm_input(self, x: torch.Tensor, norm_key: str, *, groups: int, eps: float, silu: bool,
+                         x2: torch.Tensor | None = None) -> torch.Tensor:
+        """``f16(silu?(GN([x | x2])))``: the affine from the producers' statistics
+        when both sources carry them, else from a statistics pass; then the
+        normalize pass."""
+        gamma, beta = self.p.f32(norm_key + ".weight"), self.p.f32(norm_key + ".bias")
+        st1 = getattr(x, _GN_STATS, None)
+        st2 = None if x2 is None else getattr(x2, _GN_STATS, None)
+        if st1 is not None and (x2 is None or st2 is not None):
+            voxels = int(x.shape[1]) * int(x.shape[2]) * int(x.shape[3])
+            affine = ops.group_norm_affine_from_stats(st1, gamma, beta, voxels=voxels, groups=groups, eps=eps,
+                                                      stats2=st2)
+        else:
+            affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=eps, x2=x2)
+        return ops.prepare_input(x, affine=affine, silu=silu, x2=x2)
 
     def norm_silu_conv(self, x: torch.Tensor, norm_key: str, conv_key: str, *, groups: int, eps: float,
                        shift: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-                       x2: torch.Tensor | None = None, output_scale: float = 1.0) -> torch.Tensor:
+                       x2: torch.Tensor | None = None, output_scale: float = 1.0, stats: bool = False
+                       ) -> torch.Tensor:
         """``residual + conv(SiLU(GN([x | x2]))) + shift`` (mlx_model.py:290-342)."""
-        affine = ops.group_norm_affine(x, self.p.f32(norm_key + ".weight"), self.p.f32(norm_key + ".bias"),
-                                       groups=groups, eps=eps, x2=x2)
-        prepared = ops.prepare_input(x, affine=affine, silu=True, x2=x2)
-        return self.conv(prepared, conv_key, residual=residual, shift=shift, output_scale=output_scale)
+        prepared = self.group_norm_input(x, norm_key, groups=groups, eps=eps, silu=True, x2=x2)
+        return self.conv(prepared, conv_key, residual=residual, shift=shift, output_scale=output_scale, stats=stats)
 
     def dense(self, x: torch.Tensor, *keys: str, residual: torch.Tensor | None = None,
               act: int = _lib.LDB_ACT_NONE) -> torch.Tensor:
@@ -212,7 +254,7 @@ class LdmUnetB200(_Layers):
         lo, hi = self._emb_offsets[key]
         shift = emb[:, lo:hi].contiguous()
         h = self.norm_silu_conv(x, key + ".in_layers.0", key + ".in_layers.2", groups=groups, eps=1e-5,
-                                shift=shift, x2=x2)
+                                shift=shift, x2=x2, stats=True)
         out_c = int(h.shape[-1])
         groups = 32 if out_c % 32 == 0 else out_c
         if self.p.has(key + ".skip_connection.weight"):
@@ -221,7 +263,7 @@ class LdmUnetB200(_Layers):
         else:
             skip = x
         return self.norm_silu_conv(h, key + ".out_layers.0", key + ".out_layers.3", groups=groups, eps=1e-5,
-                                   residual=skip)
+                                   residual=skip, stats=True)
 
     def attention(self, x: torch.Tensor, key: str, heads: int, kv: tuple[torch.Tensor, torch.Tensor] | None,
                   residual: torch.Tensor) -> torch.Tensor:
@@ -241,9 +283,7 @@ class LdmUnetB200(_Layers):
         """mlx_model.py:522-552 on NDHWC tokens."""
         b = int(x.shape[0])
         c = int(x.shape[-1])
-        affine = ops.group_norm_affine(x, self.p.f32(key + ".norm.weight"), self.p.f32(key + ".norm.bias"),
-                                       groups=32, eps=1e-6)
-        normed = ops.prepare_input(x, affine=affine)
+        normed = self.group_norm_input(x, key + ".norm", groups=32, eps=1e-6, silu=False)
         t = self.conv(normed, key + ".proj_in")
         tokens = t.view(b, -1, c)
         heads = c // self.config.num_head_channels
@@ -256,7 +296,7 @@ class LdmUnetB200(_Layers):
         tokens = self.attention(ln(tokens, "norm2"), blk + ".attn2", heads, cache.get(blk + ".attn2"), tokens)
         ff = self.dense(ln(tokens, "norm3"), blk + ".ff.net.0.0", act=_lib.LDB_ACT_GELU)
         tokens = self.dense(ff, blk + ".ff.net.2", residual=tokens)
-        return self.conv(tokens.view(t.shape), key + ".proj_out", residual=x)
+        return self.conv(tokens.view(t.shape), key + ".proj_out", residual=x, stats=True)
 
     def prepare_context(self, context: torch.Tensor | None) -> dict:
         """Project the context and every attn2 K/V once per binding (mlx_model.py:570-597)."""
@@ -280,7 +320,8 @@ class LdmUnetB200(_Layers):
         """Noise prediction for NDHWC f16 ``x`` (B, D, H, W, C_in) (mlx_model.py:599-654)."""
         cfg = self.config
         emb = self.block_shifts(self.time_embedding(timesteps, step))
-        h = self.conv(x, "input_blocks.0.0")
+        self._begin_stats(int(x.shape[0]), x.device)
+        h = self.conv(x, "input_blocks.0.0", stats=True)
         skips = [h]
         block, resolution = 1, 1
         for level in range(len(cfg.channel_mult)):
@@ -292,7 +333,7 @@ class LdmUnetB200(_Layers):
                 skips.append(h)
                 block += 1
             if level < len(cfg.channel_mult) - 1:
-                h = self.conv(h, f"input_blocks.{block}.0.op", stride=2)
+                h = self.conv(h, f"input_blocks.{block}.0.op", stride=2, stats=True)
                 skips.append(h)
                 block += 1
                 resolution *= 2
@@ -308,11 +349,13 @@ class LdmUnetB200(_Layers):
                 if has_attention:
                     h = self.transformer(h, key + ".1", cache)
                 if level and i == cfg.num_res_blocks:
-                    h = self.conv(h, key + f".{2 if has_attention else 1}.conv")
+                    h = self.conv(h, key + f".{2 if has_attention else 1}.conv", stats=True)
                     resolution //= 2
                 block += 1
         groups = 32 if h.shape[-1] % 32 == 0 else int(h.shape[-1])
-        return self.norm_silu_conv(h, "out.0", "out.2", groups=groups, eps=1e-5)
+        out = self.norm_silu_conv(h, "out.0", "out.2", groups=groups, eps=1e-5)
+        self._arena = None
+        return out
 
     def __call__(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor | None) -> torch.Tensor:
         return self.forward(x, timesteps, self.prepare_context(context))

@@ -101,6 +101,31 @@ def prepare_input(
     return out if split else out[..., :channels]
 
 
+def group_norm_affine_from_stats(
+    stats: torch.Tensor, gamma: torch.Tensor | None, beta: torch.Tensor | None, *, voxels: int, groups: int,
+    eps: float, stats2: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``group_norm_affine`` from producer statistics: float64 ``(B, C, 2)`` sums
+    and sums of squares per source (as ``conv3d_ndhwc(..., stats=...)``
+    accumulates them) over ``voxels`` voxels per batch item."""
+    if stats.dtype != torch.float64 or stats.ndim != 3 or stats.shape[2] != 2 or not stats.is_contiguous():
+        raise ValueError("stats must be a contiguous float64 (B, C, 2) tensor")
+    batch, c1 = int(stats.shape[0]), int(stats.shape[1])
+    c2 = 0
+    if stats2 is not None:
+        if stats2.dtype != torch.float64 or stats2.shape[0] != batch or not stats2.is_contiguous():
+            raise ValueError("stats2 must be a contiguous float64 (B, C2, 2) tensor")
+        c2 = int(stats2.shape[1])
+    affine = torch.empty((batch, c1 + c2, 2), dtype=torch.float32, device=stats.device)
+    g = None if gamma is None else gamma.to(torch.float32).contiguous()
+    b = None if beta is None else beta.to(torch.float32).contiguous()
+    with instrument.maybe_time("group_norm", 0.0):
+        _lib.call("ldb_group_norm_affine_from_stats", torch.cuda.current_stream(stats.device).cuda_stream,
+                  stats.data_ptr(), c1, _ptr(stats2), c2, batch, int(voxels), groups, _ptr(g), _ptr(b), float(eps),
+                  affine.data_ptr())
+    return affine
+
+
 def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """Last-axis LayerNorm of f16 rows; ``gamma``/``beta`` f32."""
