@@ -215,15 +215,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(tmem_s + c0, chunk);
       }
       tmem_wait_ld();
-      float mx = -INFINITY;
-      if (valid == kBlockN) {
-#pragma unroll
-        for (int i = 0; i < kBlockN; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-      } else {
+      const bool full = valid == kBlockN;
+      if (!full) {
+        // keys past the end never count: -inf scores give zero probability
 #pragma unroll
         for (int i = 0; i < kBlockN; ++i)
-          if (i < valid) mx = fmaxf(mx, __uint_as_float(sr[i]));
+          if (i >= valid) sr[i] = __float_as_uint(-INFINITY);
       }
+      // row maximum as 8 independent chains folded by a tree
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(sr[k]);
+#pragma unroll
+      for (int i = 8; i < kBlockN; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(sr[i + k]));
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const bool first = j == 0;
       const bool grow = first || (mx - m_ref) * c > kRescaleLog2;
       const float m_new = grow ? fmaxf(m_ref, mx) : m_ref;
@@ -255,15 +263,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_ref = m_new;
       }
       const float mc = m_ref * c;
-      float sum = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
 #pragma unroll
       for (int c0 = 0; c0 < kBlockN; c0 += 32) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = (c0 + i < valid) ? exp2f(fmaf(__uint_as_float(sr[c0 + i]), c, -mc)) : 0.f;
-          const float e1 = (c0 + i + 1 < valid) ? exp2f(fmaf(__uint_as_float(sr[c0 + i + 1]), c, -mc)) : 0.f;
-          sum += e0 + e1;
+          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c0 + i]), c, -mc));
+          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c0 + i + 1]), c, -mc));
+          s4[(i >> 1) & 3] += e0 + e1;
           if constexpr (BF16) {
             __nv_bfloat162 v2 = __floats2bfloat162_rn(e0, e1);
             packed[i / 2] = *reinterpret_cast<uint32_t*>(&v2);
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
         }
       }
-      l += sum;
+      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

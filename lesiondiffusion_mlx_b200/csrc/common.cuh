@@ -121,6 +121,15 @@ __device__ __forceinline__ void pdl_begin() {
   pdl_trigger();
 }
 
+// 2^x by the hardware approximation (MUFU ex2; relative error about 2^-22,
+// results below the FP32 normal range flush to zero), for softmax
+// probabilities that are rounded to 16 bits afterwards.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Fire-and-forget FP64 add to global memory (no value returned, so the
 // thread does not wait for the L2 round trip).
 __device__ __forceinline__ void red_add_f64(double* addr, double v) {
