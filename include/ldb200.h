@@ -101,6 +101,12 @@ typedef struct {
   int out_dtype;    /* LDB_F16 or LDB_F32 */
   int act;          /* LDB_ACT_* */
   float output_scale;
+  /* Depth halo: the first and last `depth_halo` of x's `depth` slices are a
+   * neighbour's slices (or zeros at the volume ends) that the 3x3x3 taps read
+   * instead of zero padding; the output covers the depth - 2 * depth_halo
+   * interior slices (twice that for LDB_CONV_UP2).  0 or 1; not with stride 2.
+   * Used by the depth-sharded decode, where each GPU holds a slab. */
+  int depth_halo;
 } ldb_conv_desc;
 
 /* Workspace bytes ldb_conv3d_fwd needs (split-K partial tiles; 0 if none). */

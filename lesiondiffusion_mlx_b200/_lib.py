@@ -46,6 +46,7 @@ class ConvDesc(ctypes.Structure):
         ("out_dtype", ctypes.c_int),
         ("act", ctypes.c_int),
         ("output_scale", ctypes.c_float),
+        ("depth_halo", ctypes.c_int),
     ]
 
 

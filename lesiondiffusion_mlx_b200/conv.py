@@ -143,21 +143,37 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _dense_ld(shape, strides, what: str) -> int:
+    """Channel stride of an NDHWC layout that is dense over voxels (only the
+    channel stride may exceed C)."""
+    if len(shape) != 5 or (strides[4] != 1 and shape[4] != 1):
+        raise ValueError(f"{what} must be (B, D, H, W, C) with unit channel stride")
+    ld = int(strides[3])
+    expect = ld
+    for dim in (3, 2, 1, 0):
+        if int(shape[dim]) != 1 and int(strides[dim]) != expect:
+            raise ValueError(f"{what} must be dense over voxels (only the channel stride may exceed C)")
+        expect *= int(shape[dim])
+    return ld
+
+
 def conv_geometry(x_shape, x_strides, packed: PackedWeight, *, stride: int = 1,
-                  in_channels: int | None = None) -> tuple[int, tuple[int, int, int], int, int]:
+                  in_channels: int | None = None, depth_halo: int = 0) -> tuple[int, tuple[int, int, int], int, int]:
     """Validate an NDHWC input layout for ``packed``; return (mode, output grid, x_ld, cin).
 
+    With ``depth_halo`` = 1 the first and last depth slices of x are halo
+    slices read by the taps and the output covers the interior slices.
     Pure host logic (no device access), shared by ``conv3d_ndhwc`` and the CPU tests.
     """
-    if len(x_shape) != 5 or (x_strides[4] != 1 and x_shape[4] != 1):
-        raise ValueError("x must be (B, D, H, W, C) with unit channel stride")
+    x_ld = _dense_ld(x_shape, x_strides, "x")
+    if depth_halo not in (0, 1):
+        raise ValueError("depth_halo must be 0 or 1")
     depth, height, width = (int(s) for s in x_shape[1:4])
-    x_ld = int(x_strides[3])
-    expect = x_ld
-    for dim in (3, 2, 1, 0):
-        if int(x_shape[dim]) != 1 and int(x_strides[dim]) != expect:
-            raise ValueError("x must be dense over voxels (only the channel stride may exceed C)")
-        expect *= int(x_shape[dim])
+    depth -= 2 * depth_halo
+    if depth <= 0:
+        raise ValueError("x has no interior depth slice")
+    if depth_halo and stride != 1:
+        raise ValueError("a depth halo needs stride 1")
     cin = packed.in_channels if in_channels is None else in_channels
     if packed.kind == "up":
         if stride != 1:
@@ -188,6 +204,7 @@ def conv3d_ndhwc(
     out_dtype: torch.dtype | None = None,
     in_channels: int | None = None,
     stats: torch.Tensor | None = None,
+    depth_halo: int = 0,
 ) -> torch.Tensor:
     """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
@@ -198,14 +215,16 @@ def conv3d_ndhwc(
     feed the next convolution.  Stride applies only to ``kind == "conv"``.
     With ``stats`` (float64 ``(B, O, 2)``, zero on entry) the kernel also adds
     each channel's sum and sum of squares of the stored output: the GroupNorm
-    statistics that ``ops.group_norm_affine_from_stats`` consumes.
+    statistics that ``ops.group_norm_affine_from_stats`` consumes.  With
+    ``depth_halo`` = 1, x's first and last depth slices are a neighbour's
+    slices (depth-sharded volumes) and the output covers the interior.
     """
     if x.device.type != "cuda":
         raise ValueError("conv3d_ndhwc needs CUDA tensors")
     if x.dtype != torch.float16:
         raise ValueError(f"conv input must be float16 (split planes for FP32), got {x.dtype}")
     mode, grid, x_ld, cin = conv_geometry(tuple(x.shape), tuple(x.stride()), packed, stride=stride,
-                                          in_channels=in_channels)
+                                          in_channels=in_channels, depth_halo=depth_halo)
     batch = int(x.shape[0])
     cout = packed.out_channels
     if out_dtype is None:
@@ -213,15 +232,15 @@ def conv3d_ndhwc(
     if out is None:
         out_ld = (cout + 7) // 8 * 8
         out = torch.empty((batch, *grid, out_ld), device=x.device, dtype=out_dtype)[..., :cout]
-    if out.dtype != out_dtype or tuple(out.shape) != (batch, *grid, cout) or (out.stride(4) != 1 and cout != 1):
-        raise ValueError(f"out must be {(batch, *grid, cout)} {out_dtype} with unit channel stride")
+    if out.dtype != out_dtype or tuple(out.shape) != (batch, *grid, cout):
+        raise ValueError(f"out must be {(batch, *grid, cout)} {out_dtype}")
+    out_ld = _dense_ld(tuple(out.shape), tuple(out.stride()), "out")
     res_ld = cout
     if residual is not None:
-        if tuple(residual.shape) != (batch, *grid, cout) or residual.dtype != out_dtype or (
-                residual.stride(4) != 1 and cout != 1):
+        if tuple(residual.shape) != (batch, *grid, cout) or residual.dtype != out_dtype:
             raise ValueError(f"residual shape {tuple(residual.shape)} {residual.dtype} != output "
                              f"{(batch, *grid, cout)} {out_dtype}")
-        res_ld = int(residual.stride(3))
+        res_ld = _dense_ld(tuple(residual.shape), tuple(residual.stride()), "residual")
     if bias is not None and (bias.dtype != torch.float32 or bias.numel() != cout or not bias.is_contiguous()):
         raise ValueError("bias must be a contiguous float32 (O,) tensor")
     if shift is not None and (shift.dtype != torch.float32 or tuple(shift.shape) != (batch, cout)
@@ -230,9 +249,9 @@ def conv3d_ndhwc(
     depth, height, width = (int(s) for s in x.shape[1:4])
     desc = _lib.ConvDesc(
         batch=batch, depth=depth, height=height, width=width, in_channels=cin, x_ld=x_ld,
-        out_channels=cout, out_ld=int(out.stride(3)), res_ld=res_ld, mode=mode, exact=int(packed.exact),
+        out_channels=cout, out_ld=out_ld, res_ld=res_ld, mode=mode, exact=int(packed.exact),
         out_dtype=_lib.LDB_F32 if out_dtype == torch.float32 else _lib.LDB_F16, act=act,
-        output_scale=float(output_scale),
+        output_scale=float(output_scale), depth_halo=depth_halo,
     )
     ws_bytes = ctypes.c_size_t(0)
     _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(ws_bytes))

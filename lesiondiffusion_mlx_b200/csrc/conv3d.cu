@@ -600,6 +600,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             y = h0 + ph + th - 1;
             z = d0 + pd + td - 1;
           }
+          z += p.in_zoff;
           tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
           tma_load_2d(sb, &wmap, &full[stage], tap * p.cin_pad + chn, brow);
           if (EXACT) {
@@ -934,11 +935,15 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   else if (cout <= 64) bn = 64;
   else if (cout <= 128 || exact) bn = 128;
   else bn = 256;
+  if (d->depth_halo < 0 || d->depth_halo > 1) return fail(LDB_ERR_SHAPE, "depth_halo must be 0 or 1");
+  if (d->depth_halo && d->mode == LDB_CONV_3X3X3_S2) return fail(LDB_ERR_SHAPE, "depth_halo with stride 2");
+  if (D - 2 * d->depth_halo <= 0) return fail(LDB_ERR_SHAPE, "depth %d leaves no interior slice", D);
   ConvParams& p = plan->p;
   p = ConvParams{};
   p.batch = B;
   p.mode = d->mode;
-  int gd = D, gh = H, gw = W;
+  p.in_zoff = d->depth_halo;
+  int gd = D - 2 * d->depth_halo, gh = H, gw = W;
   if (d->mode == LDB_CONV_3X3X3_S2) {
     gd = (D - 1) / 2 + 1;
     gh = (H - 1) / 2 + 1;

@@ -32,6 +32,7 @@ struct ConvParams {
   int cin_pad;       // weight channels per tap (multiple of the K block)
   int taps;
   int mode;
+  int in_zoff;           // depth index of output slice 0's centre tap in x (the depth halo)
   int wrows_per_parity;  // packed weight rows per parity (Cout padded to BN)
   int num_tiles;         // batch * tiles * parities * n_tiles * k_splits
   // Epilogue: out = act((acc + bias + shift[b]) * scale + residual), stored as

@@ -394,10 +394,10 @@ class VqDecoderB200(_Layers):
     def residual(self, x: torch.Tensor, key: str, scaled_in: bool = False, scaled_out: bool = False) -> torch.Tensor:
         """mlx_model.py:720-727 (+ _scaled_vq.py:75-118 scaling)."""
         eps1 = 1e-6 * (self.SCALE ** 2 if scaled_in else 1.0)
-        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=self.groups, eps=eps1)
+        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=self.groups, eps=eps1, stats=True)
         skip = self.conv(x, key + ".nin_shortcut") if self.p.has(key + ".nin_shortcut.weight") else x
         return self.norm_silu_conv(h, key + ".norm2", key + ".conv2", groups=self.groups, eps=1e-6, residual=skip,
-                                   output_scale=self.SCALE if scaled_out else 1.0)
+                                   output_scale=self.SCALE if scaled_out else 1.0, stats=True)
 
     def quantize(self, z: torch.Tensor) -> torch.Tensor:
         """Nearest code + straight-through value (mlx_model.py:742-803)."""
@@ -410,8 +410,9 @@ class VqDecoderB200(_Layers):
     def decode(self, z: torch.Tensor, *, quantize: bool = True, to_hu: bool = False) -> torch.Tensor:
         """Decode NDHWC f16 latent ``z`` (B, d, h, w, C) to (B, 2d, 2h, 2w, C_out) (mlx_model.py:805-819)."""
         x = self.quantize(z) if quantize else z
+        self._begin_stats(int(z.shape[0]), z.device)
         x = self.conv(x, "post_quant_conv")
-        x = self.conv(x, "decoder.conv_in")
+        x = self.conv(x, "decoder.conv_in", stats=True)
         x = self.residual(x, "decoder.mid.block_1")
         x = self.residual(x, "decoder.mid.block_2")
         upsampled = False
@@ -421,8 +422,9 @@ class VqDecoderB200(_Layers):
                 x = self.residual(x, key, scaled_in=self.scaled and upsampled, scaled_out=self.scaled and upsampled)
             if self.p.has(f"decoder.up.{level}.upsample.conv.weight"):
                 x = self.conv(x, f"decoder.up.{level}.upsample.conv",
-                              output_scale=self.SCALE if self.scaled else 1.0)
+                              output_scale=self.SCALE if self.scaled else 1.0, stats=True)
                 upsampled = True
         eps = 1e-6 * (self.SCALE ** 2 if self.scaled else 1.0)
         out = self.norm_silu_conv(x, "decoder.norm_out", "decoder.conv_out", groups=self.groups, eps=eps)
+        self._arena = None
         return ops.hu_map(out) if to_hu else out

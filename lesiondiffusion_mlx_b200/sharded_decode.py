@@ -1,0 +1,217 @@
+"""Depth-sharded VQ decode (the large-volume decode spread over several GPUs).
+
+The decoder of ``networks.VqDecoderB200`` (reference: mlx_model.py:720-727,
+:805-819) is split along depth: every GPU holds a contiguous slab of the
+latent depth and produces the matching slab of the output.  Two things cross
+slab boundaries:
+
+* every 3x3x3 convolution (and the folded 2x upsampling conv) reads one depth
+  slice beyond each end of its slab.  Activations live in buffers with one
+  halo slice on each side; before such a conv the boundary slices are sent to
+  the neighbours (grouped NCCL send/recv), and the conv reads the halo through
+  ``depth_halo = 1`` instead of zero padding.  At the two ends of the volume
+  the halo stays zero, which is the zero padding of the unsharded conv;
+* every GroupNorm normalizes over the whole volume (medmlx.py:87-88): each
+  producing conv accumulates its slab's per-channel sums (``stats``), the
+  slabs' sums are all-reduced, and the affine uses the global voxel count.
+
+Quantization and the HU map are per voxel and need no exchange.
+
+The decode runs over a *list* of slabs with a communicator, so the same code
+serves one slab per process (``DistDepthComm`` over torch.distributed, NCCL
+on GPUs, gloo on CPU) and all slabs in one process (``LocalDepthComm``, which
+emulates the ranks on one GPU so the sharding can be checked against the
+unsharded decode).  Batch size 1 (one volume).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+from .conv import conv3d_ndhwc
+from .networks import VqDecoderB200
+
+
+def partition_depth(depth: int, parts: int) -> list[tuple[int, int]]:
+    """Contiguous [start, stop) slabs of ``depth`` slices, sizes differing by at most one."""
+    if parts <= 0 or depth < parts:
+        raise ValueError(f"cannot split {depth} slices into {parts} non-empty slabs")
+    base, extra = divmod(depth, parts)
+    out, start = [], 0
+    for i in range(parts):
+        stop = start + base + (1 if i < extra else 0)
+        out.append((start, stop))
+        start = stop
+    return out
+
+
+class LocalDepthComm:
+    """All slabs in this process: halo exchange by copies, statistics summed."""
+
+    def exchange(self, bufs: list[torch.Tensor]) -> None:
+        """``bufs[i]`` (1, d_i + 2, H, W, ld): fill the halo slices from the neighbours."""
+        for i, buf in enumerate(bufs):
+            if i > 0:
+                buf[:, 0].copy_(bufs[i - 1][:, -2])
+            if i + 1 < len(bufs):
+                buf[:, -1].copy_(bufs[i + 1][:, 1])
+
+    def all_reduce(self, stats: list[torch.Tensor]) -> None:
+        total = stats[0].clone()
+        for s in stats[1:]:
+            total += s
+        for s in stats:
+            s.copy_(total)
+
+
+class DistDepthComm:
+    """One slab per process, neighbours are ranks r - 1 and r + 1 of ``group``."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def _peer(self, r: int) -> int:
+        return self.dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    def exchange(self, bufs: list[torch.Tensor]) -> None:
+        (buf,) = bufs
+        dist = self.dist
+        p2p = []
+        # Same order on every rank: towards rank - 1 first, then towards rank + 1.
+        if self.rank > 0:
+            p2p.append(dist.P2POp(dist.isend, buf[:, 1].contiguous(), self._peer(self.rank - 1), self.group))
+            lo = torch.empty_like(buf[:, 0])
+            p2p.append(dist.P2POp(dist.irecv, lo, self._peer(self.rank - 1), self.group))
+        if self.rank + 1 < self.world:
+            p2p.append(dist.P2POp(dist.isend, buf[:, -2].contiguous(), self._peer(self.rank + 1), self.group))
+            hi = torch.empty_like(buf[:, -1])
+            p2p.append(dist.P2POp(dist.irecv, hi, self._peer(self.rank + 1), self.group))
+        if not p2p:
+            return
+        for req in dist.batch_isend_irecv(p2p):
+            req.wait()
+        if self.rank > 0:
+            buf[:, 0].copy_(lo)
+        if self.rank + 1 < self.world:
+            buf[:, -1].copy_(hi)
+
+    def all_reduce(self, stats: list[torch.Tensor]) -> None:
+        (s,) = stats
+        self.dist.all_reduce(s, group=self.group)
+
+
+class _Slab:
+    """An activation slab: (1, d + 2, H, W, ld) buffer with zero halo slices.
+    ``x`` is the interior, ``full`` the whole buffer (halo included),
+    ``stats`` the GroupNorm sums of the interior when its producer made them."""
+
+    def __init__(self, depth: int, height: int, width: int, channels: int, dtype, device):
+        ld = (channels + 7) // 8 * 8
+        self.buf = torch.zeros((1, depth + 2, height, width, ld), dtype=dtype, device=device)
+        self.channels = channels
+        self.stats: torch.Tensor | None = None
+
+    @property
+    def full(self) -> torch.Tensor:
+        return self.buf[..., : self.channels]
+
+    @property
+    def x(self) -> torch.Tensor:
+        return self.buf[:, 1:-1, ..., : self.channels]
+
+
+class ShardedVqDecoder:
+    """``VqDecoderB200.decode`` over depth slabs (see the module docstring).
+
+    ``decode`` takes the slabs this process holds (one per rank with
+    ``DistDepthComm``, all of them with ``LocalDepthComm``) and the latent
+    depth of the whole volume, and returns the output slabs.
+    """
+
+    def __init__(self, decoder: VqDecoderB200, comm):
+        self.dec = decoder
+        self.p = decoder.p
+        self.comm = comm
+
+    # ------------------------------------------------------------ primitives
+
+    def _new(self, like: list[_Slab], channels: int, scale: int = 1) -> list[_Slab]:
+        return [_Slab(scale * s.x.shape[1], scale * s.x.shape[2], scale * s.x.shape[3], channels, s.buf.dtype,
+                      s.buf.device) for s in like]
+
+    def _conv(self, src: list[_Slab], key: str, *, halo: bool, residual: list[_Slab] | None = None,
+              output_scale: float = 1.0, stats: bool = True) -> list[_Slab]:
+        """Conv ``key`` of every slab into new slabs; 3x3x3 / up convs read the halo."""
+        packed = self.p.conv(key)
+        up = 2 if packed.kind == "up" else 1
+        if halo:
+            self.comm.exchange([s.buf for s in src])
+        out = self._new(src, packed.out_channels, up)
+        for i, (s, o) in enumerate(zip(src, out)):
+            if stats:
+                o.stats = torch.zeros((1, packed.out_channels, 2), dtype=torch.float64, device=s.buf.device)
+            conv3d_ndhwc(s.full if halo else s.x, packed, self.p.f32(key + ".bias"), out=o.x,
+                         residual=None if residual is None else residual[i].x, output_scale=output_scale,
+                         stats=o.stats, depth_halo=1 if halo else 0)
+        return out
+
+    def _norm(self, src: list[_Slab], key: str, *, eps: float, voxels: int) -> list[_Slab]:
+        """GroupNorm + SiLU of every slab over the whole volume into new slabs."""
+        self.comm.all_reduce([s.stats for s in src])
+        gamma, beta = self.p.f32(key + ".weight"), self.p.f32(key + ".bias")
+        out = self._new(src, src[0].channels)
+        for s, o in zip(src, out):
+            affine = ops.group_norm_affine_from_stats(s.stats, gamma, beta, voxels=voxels, groups=self.dec.groups,
+                                                      eps=eps)
+            ops.prepare_input(s.x, affine=affine, silu=True, out=o.x)
+        return out
+
+    def _residual(self, x: list[_Slab], key: str, voxels: int, scaled_in: bool, scaled_out: bool) -> list[_Slab]:
+        s = self.dec.SCALE
+        h = self._norm(x, key + ".norm1", eps=1e-6 * (s * s if scaled_in else 1.0), voxels=voxels)
+        h = self._conv(h, key + ".conv1", halo=True)
+        skip = self._conv(x, key + ".nin_shortcut", halo=False, stats=False) \
+            if self.p.has(key + ".nin_shortcut.weight") else x
+        h = self._norm(h, key + ".norm2", eps=1e-6, voxels=voxels)
+        return self._conv(h, key + ".conv2", halo=True, residual=skip, output_scale=s if scaled_out else 1.0)
+
+    # ------------------------------------------------------------ decode
+
+    def decode(self, z_slabs: list[torch.Tensor], latent_depth: int, *, quantize: bool = True,
+               to_hu: bool = False) -> list[torch.Tensor]:
+        """Decode NDHWC f16 latent slabs (1, d_i, h, w, C) of a volume with
+        ``latent_depth`` slices; returns the output slabs (1, s * d_i, ...)."""
+        dec = self.dec
+        if any(int(z.shape[0]) != 1 for z in z_slabs):
+            raise ValueError("the sharded decode handles one volume (batch 1)")
+        _, _, hh, ww, c = (int(v) for v in z_slabs[0].shape)
+        voxels = latent_depth * hh * ww
+        x = []
+        for z in z_slabs:
+            s = _Slab(int(z.shape[1]), hh, ww, c, torch.float16, z.device)
+            s.x.copy_(dec.quantize(z) if quantize else z)
+            x.append(s)
+        x = self._conv(x, "post_quant_conv", halo=False, stats=False)
+        x = self._conv(x, "decoder.conv_in", halo=True)
+        x = self._residual(x, "decoder.mid.block_1", voxels, False, False)
+        x = self._residual(x, "decoder.mid.block_2", voxels, False, False)
+        upsampled = False
+        for level in dec.levels:
+            for block in dec.blocks[level]:
+                scaled = dec.scaled and upsampled
+                x = self._residual(x, f"decoder.up.{level}.block.{block}", voxels, scaled, scaled)
+            if self.p.has(f"decoder.up.{level}.upsample.conv.weight"):
+                x = self._conv(x, f"decoder.up.{level}.upsample.conv", halo=True,
+                               output_scale=dec.SCALE if dec.scaled else 1.0)
+                voxels *= 8
+                upsampled = True
+        eps = 1e-6 * (dec.SCALE ** 2 if dec.scaled else 1.0)
+        h = self._norm(x, "decoder.norm_out", eps=eps, voxels=voxels)
+        out = self._conv(h, "decoder.conv_out", halo=True, stats=False)
+        return [ops.hu_map(o.x) if to_hu else o.x for o in out]

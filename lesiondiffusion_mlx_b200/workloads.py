@@ -162,6 +162,20 @@ def vq_decoder_weights(widths: tuple[int, ...], upsample_after: tuple[int, ...],
     return w
 
 
+# Config 4 (VQ decode): decoder widths 512 / 256 / 128 / 64 in execution order
+# with a 2x nearest upsample after the first two levels, 8-channel latent, one
+# output channel; 4a is the 32x40x40 latent on one GPU, 4b the 62x110x110
+# latent sharded along depth.  GroupNorm groups 32 (BASELINE) for these shapes.
+CONFIG4_WIDTHS = (512, 256, 128, 64)
+CONFIG4_UPSAMPLE_AFTER = (0, 1)
+CONFIG4_LATENTS = {"4a": (1, 8, 32, 40, 40), "4b": (1, 8, 62, 110, 110)}
+
+
+def config4_decoder_weights(seed: int = 200) -> dict[str, np.ndarray]:
+    return vq_decoder_weights(CONFIG4_WIDTHS, CONFIG4_UPSAMPLE_AFTER, latent_channels=8, out_channels=1,
+                              codebook_size=512, seed=seed)
+
+
 def config3_inputs(seed: int = 101, batch: int = 1) -> dict[str, np.ndarray]:
     """Seeded config-3 inputs: noise latent with the mask channel last, context, timesteps.
 
