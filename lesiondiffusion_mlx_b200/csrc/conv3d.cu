@@ -27,6 +27,7 @@
 // reference's SPLIT/reduce kernels (_nax_conv.py:277-289, :556-563).
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -172,24 +173,28 @@ __device__ __forceinline__ void store_outputs(const ConvParams& p, int b, long l
   }
 }
 
-template <int KC, int BN, bool EXACT>
+// TRANS: channel-major tile (activation rows are the MMA's N operand, up to
+// 256 voxels; the weight tile is the M = 128 operand).
+template <int KC, int BN, bool EXACT, bool TRANS = false>
 struct ConvCfg {
   static constexpr int kSwizzleBytes = KC * 2;  // one K block row = 32/64/128 B
   static constexpr uint32_t kLayout = KC == 64 ? kSwizzle128 : (KC == 32 ? kSwizzle64 : kSwizzle32);
   static constexpr uint32_t kSbo = 8 * KC * 2;  // bytes between 8-row groups
   static constexpr int kPlanes = EXACT ? 2 : 1;
-  static constexpr int kABytes = kTileM * KC * 2;
+  static constexpr int kRowsA = TRANS ? 256 : kTileM;  // activation rows per stage
+  static constexpr int kABytes = kRowsA * KC * 2;
   static constexpr int kBBytesRaw = BN * KC * 2;
   static constexpr int kBBytes = ((kBBytesRaw + 1023) / 1024) * 1024;
   static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
   // Epilogue staging: 2 output + 2 residual buffers of 128 rows x 128 bytes.
   static constexpr int kEpiBufBytes = kTileM * 128;
   static constexpr int kEpiBytes = 4 * kEpiBufBytes;
-  // Per-CTA GroupNorm statistics accumulator: [BN][2] FP32 shifted sums.
-  static constexpr int kStatsBytes = BN * 8;
+  // Per-CTA GroupNorm statistics accumulator: [BN][2] FP32 shifted sums
+  // (the channel-major tile keeps its sums in registers).
+  static constexpr int kStatsBytes = TRANS ? 0 : BN * 8;
   static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048 - kStatsBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
-  static constexpr int kAccCols = BN * kPlanes;
+  static constexpr int kAccCols = TRANS ? 256 : BN * kPlanes;
   static constexpr int kTmemColsRaw = 2 * kAccCols;
   static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
   // Output element size (f32 in exact mode, f16 otherwise) and the columns
@@ -203,6 +208,7 @@ struct ConvCfg {
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kEpiBytes + 1024 /*align slack*/ + kBarrierBytes + 64 + BN * 4 + kStatsBytes;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+  static_assert(!TRANS || (BN == 128 && !EXACT), "channel-major tiles are f16 with 128 channel rows");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
 };
 
@@ -216,6 +222,9 @@ struct EpiState {
   int key_b = -1;        // (batch, column tile) of the run: tiles of one run share bsum
   int key_nt = -1;
   int run_rows = 0;      // valid rows (voxels) accumulated in the run
+  float run_s1 = 0.f;    // channel-major tile: this thread's channel sums of x - k, (x - k)^2
+  float run_s2 = 0.f;
+  float run_k = 0.f;
   volatile int* abort_flag;
   unsigned int* status;
   int quarter, row;
@@ -487,11 +496,133 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
   return ok;
 }
 
-template <int KC, int BN, bool EXACT>
+// Channel-major tile: TMEM lane = output channel (the warp with quarter q
+// owns channels 32q .. 32q + 31), column = voxel of the bd x 8 x 8 brick, so
+// each depth plane of the brick is 64 consecutive columns.  Per plane: load
+// the plane's 64 sums of this thread's channel, add bias + shift, scale, the
+// residual (TMA-prefetched plane, read transposed), optional GELU, round
+// once, write each value into the swizzled staging rows [voxel][channel],
+// and store the plane with one TMA store per 64 channels.  GroupNorm
+// statistics: the thread owns one channel, so it sums x - k and (x - k)^2
+// over the run's valid voxels in registers (k = its bias + shift) and adds
+// FP64 totals when the batch item changes or the CTA ends.
+__device__ __forceinline__ void flush_trans_stats(const ConvParams& p, EpiState& st) {
+  if (st.key_b >= 0 && st.run_rows > 0 && st.row < p.cout) {
+    const double n = st.run_rows, k = st.run_k, s1 = st.run_s1, s2 = st.run_s2;
+    double* dst = p.stats + (static_cast<long long>(st.key_b) * p.cout + st.row) * 2;
+    red_add_f64(dst, s1 + n * k);
+    red_add_f64(dst + 1, s2 + 2.0 * k * s1 + n * k * k);
+  }
+  st.run_rows = 0;
+  st.run_s1 = st.run_s2 = 0.f;
+}
+
+template <class Cfg>
+__device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const ConvMaps& maps, const TileCoord& c,
+                                                    uint32_t tbase, uint64_t* acc_full_bar, uint32_t acc_parity,
+                                                    EpiState& st) {
+  const int ch = st.row;  // output channel of this thread (one column tile: n0 = 0)
+  const bool live = ch < p.cout;
+  const int w0 = c.tw * 8, h0 = c.th * 8, d0 = c.td * p.bd;
+  const int omap = p.mode == kConvUp2 ? c.par : 0;
+  const int nboxes = (p.cout + 63) / 64;
+  constexpr uint32_t kBoxBytes = 64 * 128;  // 64 voxels x 64 channels x 2 B
+  const uint32_t res_bytes = static_cast<uint32_t>(nboxes) * kBoxBytes;
+  const bool has_res = p.residual != nullptr;
+  uint8_t* const res_base = st.epi + 2 * Cfg::kEpiBufBytes;
+  auto prefetch_res = [&](int pl, int rb) {
+    mbar_arrive_expect_tx(&st.res_full[rb], res_bytes);
+    for (int bx = 0; bx < nboxes; ++bx)
+      tma_load_5d(res_base + rb * Cfg::kEpiBufBytes + bx * kBoxBytes, &maps.r[omap], &st.res_full[rb], bx * 64, w0,
+                  h0, d0 + pl, c.b);
+  };
+  if (has_res && st.leader) prefetch_res(0, st.rq & 1);
+  // valid voxels of a plane of this brick: lh < nh and lw < nw
+  const int nh = min(8, p.grid_h - h0), nw = min(8, p.grid_w - w0);
+  uint64_t plane_mask = 0;
+  for (int lh = 0; lh < nh; ++lh) plane_mask |= ((nw >= 8 ? 0xffull : ((1ull << nw) - 1))) << (8 * lh);
+  float add = 0.f;
+  if (live) {
+    if (p.bias) add = p.bias[ch];
+    if (p.shift) add += p.shift[static_cast<long long>(c.b) * p.cout + ch];
+  }
+  if (p.stats && c.b != st.key_b) {
+    flush_trans_stats(p, st);
+    st.key_b = c.b;
+    st.key_nt = 0;
+    st.run_k = add;
+  }
+  bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
+  tc_fence_after();
+  const uint32_t col_off = static_cast<uint32_t>(ch & 63) * 2;
+  const uint32_t box_off = static_cast<uint32_t>(ch >> 6) * kBoxBytes;
+#pragma unroll 1
+  for (int pl = 0; pl < p.bd; ++pl) {
+    uint8_t* ob = st.epi + (st.oq & 1) * Cfg::kEpiBufBytes;
+    if (st.leader) {
+      bulk_wait_group_read<1>();  // the stores issued two planes ago have read this buffer
+      if (has_res && pl + 1 < p.bd) prefetch_res(pl + 1, (st.rq + 1) & 1);
+    }
+    named_barrier(1, 128);
+    float v[64];
+    {
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tbase + pl * 64, r0);
+      tmem_ld32(tbase + pl * 64 + 32, r1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = __uint_as_float(r0[j]);
+        v[32 + j] = __uint_as_float(r1[j]);
+      }
+    }
+    const uint8_t* rbuf = nullptr;
+    if (has_res) {
+      const int rb = st.rq & 1;
+      uint32_t& uses = rb ? st.res_uses1 : st.res_uses0;
+      if (!mbar_wait(&st.res_full[rb], uses & 1, st.abort_flag, st.status)) ok = false;
+      uses += 1;
+      st.rq += 1;
+      rbuf = res_base + rb * Cfg::kEpiBufBytes;
+    }
+    const bool dvalid = d0 + pl < p.grid_d;
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const uint32_t off = box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128);
+      float y = (v[j] + add) * p.out_scale;
+      if (rbuf) y += __half2float(*reinterpret_cast<const __half*>(rbuf + off));
+      if (p.act == kActGelu) y = gelu_erf_f32(__half2float(__float2half_rn(y)));
+      const __half h = __float2half_rn(y);
+      if (live) *reinterpret_cast<__half*>(ob + off) = h;
+      if (dvalid && ((plane_mask >> j) & 1ull)) {
+        const float d = __half2float(h) - st.run_k;
+        s1 += d;
+        s2 = fmaf(d, d, s2);
+      }
+    }
+    if (p.stats && dvalid) {
+      st.run_s1 += s1;
+      st.run_s2 += s2;
+      st.run_rows += __popcll(plane_mask);
+    }
+    fence_proxy_async_smem();
+    named_barrier(1, 128);
+    if (st.leader) {
+      for (int bx = 0; bx < nboxes; ++bx)
+        tma_store_5d(&maps.o[omap], ob + bx * kBoxBytes, bx * 64, w0, h0, d0 + pl, c.b);
+      bulk_commit_group();
+    }
+    st.oq += 1;
+  }
+  return ok;
+}
+
+template <int KC, int BN, bool EXACT, bool TRANS>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv3d_tc_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ CUtensorMap wmap,
                      const ConvParams p, unsigned int* status) {
-  using Cfg = ConvCfg<KC, BN, EXACT>;
+  using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + Cfg::kStages * Cfg::kStageBytes;  // out[2] | res[2], 1024-aligned
@@ -650,6 +781,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
             const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
             const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            if constexpr (TRANS) {
+              // out^T: the weight tile is the M = 128 operand, the voxels are N
+              umma_ss(d_hi, bd, ad, make_idesc_f16(128, p.trans_n, 0, 0, 0), accum);
+              continue;
+            }
             umma_ss(d_hi, ad, bd, Cfg::kIdesc, accum);
             if (EXACT) {
               const uint64_t ad_lo = make_smem_desc(a_addr + Cfg::kABytes + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
@@ -692,7 +828,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int acc = local & 1;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(st.quarter * 32) << 16) + acc * Cfg::kAccCols;
       bool ok;
-      if (split) {
+      if constexpr (TRANS) {
+        ok = epilogue_tile_trans<Cfg>(p, maps, c, tbase, &acc_full[acc], (local >> 1) & 1, st);
+      } else if (split) {
         ok = epilogue_tile<Cfg, BN, EXACT, Cfg::kPartChunk, true>(p, maps, c, tbase, &acc_full[acc], (local >> 1) & 1, st);
       } else {
         ok = epilogue_tile<Cfg, BN, EXACT, Cfg::kOutChunk, false>(p, maps, c, tbase, &acc_full[acc], (local >> 1) & 1, st);
@@ -702,7 +840,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
-    if (p.stats && !split && st.key_b >= 0) {
+    if constexpr (TRANS) {
+      if (p.stats) flush_trans_stats(p, st);
+    } else if (p.stats && !split && st.key_b >= 0) {
       named_barrier(1, 128);
       flush_stats<BN>(p, st, false);
     }
@@ -858,11 +998,11 @@ void choose_brick(int d, int h, int w, bool pointwise, int* bd, int* bh, int* bw
   *bw = best[2];
 }
 
-template <int KC, int BN, bool EXACT>
+template <int KC, int BN, bool EXACT, bool TRANS = false>
 int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wmap, const ConvParams& p,
                 int grid) {
-  using Cfg = ConvCfg<KC, BN, EXACT>;
-  auto kernel = conv3d_tc_kernel<KC, BN, EXACT>;
+  using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
+  auto kernel = conv3d_tc_kernel<KC, BN, EXACT, TRANS>;
   int smem = Cfg::kSmemBytes;
   // Keep one CTA per SM when the accumulators need more than half of TMEM,
   // so co-resident CTAs never queue on tcgen05.alloc.
@@ -903,6 +1043,15 @@ int dispatch_bn(int bn, cudaStream_t stream, const ConvMaps& maps, const CUtenso
       break;
   }
   return fail(LDB_ERR_SHAPE, "no conv kernel for BN=%d", bn);
+}
+
+// The channel-major tile is on unless LDB_CONV_TRANS=0 (for comparisons).
+bool conv_trans_enabled() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("LDB_CONV_TRANS");
+    return !(v && v[0] == '0');
+  }();
+  return enabled;
 }
 
 struct ConvPlan {
@@ -990,6 +1139,38 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   plan->bn = bn;
   plan->taps = taps;
   plan->cin_pad = cin_pad;
+  // Channel-major tile for 64 / 128 output channels when the grid needs no
+  // split-K: the MMA runs as 128 (channels) x 64*bd (voxels of a bd x 8 x 8
+  // brick), the efficient 128 x 256 shape at bd = 4 where a 128-channel
+  // voxel-major tile would run 128 x 128.  bd minimises waves x tile size.
+  // (64-channel K blocks only: with 16 / 32 input channels per block the
+  // per-block overhead dominates and the voxel-major tile is faster.)
+  const bool trans_ok = !exact && p.k_splits == 1 && kc == 64 &&
+                        (cout == 128 || (cout == 64 && p.parities == 1)) && conv_trans_enabled();
+  if (trans_ok) {
+    const long long th = (gh + 7) / 8, tw = (gw + 7) / 8;
+    int best_bd = 1;
+    long long best_cost = -1;
+    for (int cand = 1; cand <= 4; ++cand) {
+      const long long tiles = static_cast<long long>(B) * ((gd + cand - 1) / cand) * th * tw * p.parities;
+      const long long cost = ((tiles + sms - 1) / sms) * (64LL * cand + 64);
+      if (best_cost < 0 || cost <= best_cost) {
+        best_cost = cost;
+        best_bd = cand;
+      }
+    }
+    p.trans = 1;
+    p.bd = best_bd;
+    p.bh = 8;
+    p.bw = 8;
+    p.trans_n = 64 * best_bd;
+    p.tiles_d = (gd + best_bd - 1) / best_bd;
+    p.tiles_h = static_cast<int>(th);
+    p.tiles_w = static_cast<int>(tw);
+    p.n_tiles = 1;  // the weight tile covers all output channels (rows past cout read as zero)
+    p.num_tiles = static_cast<int>(static_cast<long long>(B) * p.tiles_d * th * tw * p.parities);
+    plan->bn = 128;
+  }
   plan->grid = static_cast<int>(std::min<long long>(p.num_tiles, sms));
   plan->workspace = p.k_splits > 1 ? static_cast<size_t>(p.num_tiles) * kTileM * bn * sizeof(float) : 0;
   return LDB_OK;
@@ -1088,8 +1269,9 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
     if (rc != LDB_OK) return rc;
   } else {
     const int cc = std::min(plan.bn, 128 / out_esz);
+    // channel-major tiles store one depth plane per TMA store
     const uint32_t obox[5] = {static_cast<uint32_t>(cc), static_cast<uint32_t>(p.bw), static_cast<uint32_t>(p.bh),
-                              static_cast<uint32_t>(p.bd), 1u};
+                              static_cast<uint32_t>(p.trans ? 1 : p.bd), 1u};
     auto encode_out = [&](CUtensorMap* dst, const void* base_ptr, int ld) -> int {
       if ((static_cast<long long>(ld) * out_esz) % 16 != 0)
         return fail(LDB_ERR_ALIGNMENT, "output/residual channel stride %d is not a multiple of 16 bytes", ld);
@@ -1138,6 +1320,13 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
   rc = encode_tiled_f16(&wmap, w_packed, 2, wdims, wstrides, wbox, plan.kc * 2);
   if (rc != LDB_OK) return rc;
 
+  if (p.trans) {
+    switch (plan.kc) {
+      case 16: return launch_conv<16, 128, false, true>(stream, maps, wmap, p, plan.grid);
+      case 32: return launch_conv<32, 128, false, true>(stream, maps, wmap, p, plan.grid);
+      default: return launch_conv<64, 128, false, true>(stream, maps, wmap, p, plan.grid);
+    }
+  }
   switch (plan.kc) {
     case 16:
       return exact ? dispatch_bn<16, true>(plan.bn, stream, maps, wmap, p, plan.grid)

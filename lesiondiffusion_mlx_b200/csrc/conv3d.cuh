@@ -32,6 +32,10 @@ struct ConvParams {
   int cin_pad;       // weight channels per tap (multiple of the K block)
   int taps;
   int mode;
+  // Channel-major tile: the MMA computes out^T (M = output channels, N =
+  // trans_n voxels of a bd x 8 x 8 brick); 0 for the voxel-major tile.
+  int trans;
+  int trans_n;
   int in_zoff;           // depth index of output slice 0's centre tap in x (the depth halo)
   int wrows_per_parity;  // packed weight rows per parity (Cout padded to BN)
   int num_tiles;         // batch * tiles * parities * n_tiles * k_splits

@@ -145,6 +145,54 @@ def test_pointwise_conv_and_gelu(cuda_device, shape, out_channels):
     assert np.all(np.abs(gelu_actual - gelu_expected) <= 2 * half_spacing(gelu_expected) + 1e-6)
 
 
+@pytest.mark.parametrize(
+    ("shape", "out_channels", "kind", "extra"),
+    [
+        ((1, 32, 24, 24, 40), 128, "conv", False),  # whole 8 x 8 planes
+        ((1, 64, 45, 21, 27), 128, "conv", True),  # ragged planes and depth; shift + residual + scale
+        ((1, 96, 41, 24, 24), 64, "conv", True),  # 64 output channels (weight rows past 64 read as zero)
+        ((1, 32, 12, 16, 16), 128, "up", False),  # folded upsampling, 8 output parities
+        ((1, 256, 30, 24, 40), 128, "pw", False),  # pointwise, two 64-channel K blocks
+    ],
+)
+def test_channel_major_tile(cuda_device, shape, out_channels, kind, extra):
+    """Convs with 64 / 128 output channels on grids that need no split-K run as
+    channel-major tiles (out^T = W x^T, transposed epilogue)."""
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_upsample_weight, pack_weight
+
+    k = 1 if kind == "pw" else 3
+    x, w, b = f16_case(shape, out_channels, k, seed=sum(shape) + out_channels)
+    wd = w.to(cuda_device)
+    packed = pack_upsample_weight(wd) if kind == "up" else pack_weight(wd)
+    xd = to_ndhwc(x.to(cuda_device))
+    batch = shape[0]
+    if kind == "up":
+        up = x.double().repeat_interleave(2, 2).repeat_interleave(2, 3).repeat_interleave(2, 4)
+        expected, mag = reference(up, w.double(), b.double(), 1, 1)
+        tol_mag = ACCUMULATION_EPS + OPERAND_ROUNDING
+    else:
+        expected, mag = reference(x.double(), w.double(), b.double(), 1, 1 if k == 3 else 0)
+        tol_mag = ACCUMULATION_EPS
+    shift = residual = None
+    scale = 1.0
+    if extra:
+        rng = np.random.default_rng(9)
+        shift_np = rng.normal(size=(batch, out_channels)).astype(np.float32)
+        res_np = rng.normal(size=expected.shape).astype(np.float16)
+        shift = torch.from_numpy(shift_np).to(cuda_device)
+        residual = to_ndhwc(torch.from_numpy(res_np).to(cuda_device)).contiguous()
+        scale = 0.5
+        expected = (expected + shift_np.astype(np.float64)[:, :, None, None, None]) * scale + res_np.astype(np.float64)
+        mag = mag * scale
+    out = conv3d_ndhwc(xd, packed, b.to(cuda_device).float(), shift=shift, residual=residual, output_scale=scale)
+    torch.cuda.synchronize()
+    actual = out.permute(0, 4, 1, 2, 3).double().cpu().numpy()
+    assert actual.shape == expected.shape
+    error = np.abs(actual - expected)
+    bound = half_spacing(expected) + tol_mag * mag
+    assert np.all(error <= bound), f"max excess {(error - bound).max()}"
+
+
 def fp32_case(shape, out_channels, seed):
     rng = np.random.default_rng(seed)
     scales = np.exp(rng.normal(size=(1, shape[1], 1, 1, 1)) * 2)
