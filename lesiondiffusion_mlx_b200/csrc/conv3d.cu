@@ -194,7 +194,12 @@ struct ConvCfg {
   static constexpr int kStatsBytes = TRANS ? 0 : BN * 8;
   static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048 - kStatsBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
-  static constexpr int kAccCols = TRANS ? 256 : BN * kPlanes;
+  // Two accumulator chains (even / odd K steps, added in the epilogue): the
+  // tensor pipe overlaps MMAs into different accumulators but serialises
+  // successive MMAs into one, which at N <= 128 leaves it idle about half of
+  // the time.  Used where TMEM holds 2 chains x 2 tile buffers.
+  static constexpr int kChains = (!EXACT && !TRANS && KC >= 32 && 4 * BN <= 512) ? 2 : 1;
+  static constexpr int kAccCols = TRANS ? 256 : BN * kPlanes * kChains;
   static constexpr int kTmemColsRaw = 2 * kAccCols;
   static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
   // Output element size (f32 in exact mode, f16 otherwise) and the columns
@@ -411,6 +416,12 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           v[s16 * 16 + j] = __uint_as_float(r[j]) + __uint_as_float(lo[j]) * (1.0f / 2048.0f);
+      } else if constexpr (Cfg::kChains == 2) {
+        uint32_t odd[16];
+        tmem_ld16(tbase + BN + c0 + s16 * 16, odd);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[s16 * 16 + j] = __uint_as_float(r[j]) + __uint_as_float(odd[j]);
       } else {
         tmem_wait_ld();
 #pragma unroll
@@ -574,6 +585,16 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
       for (int j = 0; j < 32; ++j) {
         v[j] = __uint_as_float(r0[j]);
         v[32 + j] = __uint_as_float(r1[j]);
+      }
+      if (p.trans_chains == 2) {  // odd K steps accumulated 128 columns further
+        tmem_ld32(tbase + 128 + pl * 64, r0);
+        tmem_ld32(tbase + 128 + pl * 64 + 32, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] += __uint_as_float(r0[j]);
+          v[32 + j] += __uint_as_float(r1[j]);
+        }
       }
     }
     const uint8_t* rbuf = nullptr;
@@ -780,10 +801,17 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           for (int k = 0; k < KC / 16; ++k) {
             const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
             const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+            const int step = (kb - kb0) * (KC / 16) + k;  // K step within the tile
             const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
             if constexpr (TRANS) {
               // out^T: the weight tile is the M = 128 operand, the voxels are N
-              umma_ss(d_hi, bd, ad, make_idesc_f16(128, p.trans_n, 0, 0, 0), accum);
+              const int chains = p.trans_chains;
+              umma_ss(d_hi + (chains == 2 ? (step & 1) * 128 : 0), bd, ad, make_idesc_f16(128, p.trans_n, 0, 0, 0),
+                      step >= chains ? 1u : 0u);
+              continue;
+            }
+            if constexpr (Cfg::kChains == 2) {
+              umma_ss(d_hi + (step & 1) * BN, ad, bd, Cfg::kIdesc, step >= 2 ? 1u : 0u);
               continue;
             }
             umma_ss(d_hi, ad, bd, Cfg::kIdesc, accum);
@@ -1164,6 +1192,7 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     p.bh = 8;
     p.bw = 8;
     p.trans_n = 64 * best_bd;
+    p.trans_chains = p.trans_n <= 128 ? 2 : 1;
     p.tiles_d = (gd + best_bd - 1) / best_bd;
     p.tiles_h = static_cast<int>(th);
     p.tiles_w = static_cast<int>(tw);

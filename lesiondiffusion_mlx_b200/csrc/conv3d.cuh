@@ -36,6 +36,7 @@ struct ConvParams {
   // trans_n voxels of a bd x 8 x 8 brick); 0 for the voxel-major tile.
   int trans;
   int trans_n;
+  int trans_chains;      // channel-major tile: 2 interleaved accumulator chains when trans_n <= 128
   int in_zoff;           // depth index of output slice 0's centre tap in x (the depth halo)
   int wrows_per_parity;  // packed weight rows per parity (Cout padded to BN)
   int num_tiles;         // batch * tiles * parities * n_tiles * k_splits
