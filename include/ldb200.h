@@ -54,7 +54,9 @@ enum {
   LDB_CONV_3X3X3 = 0,    /* 3x3x3, padding 1, stride 1 */
   LDB_CONV_3X3X3_S2 = 1, /* 3x3x3, padding 1, stride 2 */
   LDB_CONV_UP2 = 2,      /* 3x3x3 of a nearest 2x upsampling, weights folded by ldb_pack_upsample_weight */
-  LDB_CONV_1X1 = 3       /* pointwise conv / dense layer over tokens */
+  LDB_CONV_1X1 = 3,      /* pointwise conv / dense layer over tokens */
+  LDB_CONV_3X3X3_S2_PAD01 = 4 /* 3x3x3, stride 2, zero padding 0 before / 1 after each axis: the VQ
+                                 encoder's downsample (lesiondiffusion_mlx/mlx_model.py:735-736) */
 };
 
 enum { LDB_ACT_NONE = 0, LDB_ACT_GELU = 1 };
@@ -104,7 +106,7 @@ typedef struct {
   /* Depth halo: the first and last `depth_halo` of x's `depth` slices are a
    * neighbour's slices (or zeros at the volume ends) that the 3x3x3 taps read
    * instead of zero padding; the output covers the depth - 2 * depth_halo
-   * interior slices (twice that for LDB_CONV_UP2).  0 or 1; not with stride 2.
+   * interior slices (twice that for LDB_CONV_UP2).  0 or 1; not with stride 2 (modes 1 and 4).
    * Used by the depth-sharded decode, where each GPU holds a slab. */
   int depth_halo;
 } ldb_conv_desc;

@@ -16,7 +16,7 @@ LIBRARY_PATH = Path(__file__).resolve().parent / "libldb200.so"
 
 LDB_OK = 0
 LDB_F16, LDB_F32, LDB_BF16 = 0, 1, 2
-LDB_CONV_3X3X3, LDB_CONV_3X3X3_S2, LDB_CONV_UP2, LDB_CONV_1X1 = 0, 1, 2, 3
+LDB_CONV_3X3X3, LDB_CONV_3X3X3_S2, LDB_CONV_UP2, LDB_CONV_1X1, LDB_CONV_3X3X3_S2_PAD01 = 0, 1, 2, 3, 4
 LDB_ACT_NONE, LDB_ACT_GELU = 0, 1
 
 

@@ -18,11 +18,12 @@ import torch
 
 from . import _lib, instrument
 
-MODE_CONV, MODE_STRIDE2, MODE_UP2, MODE_POINTWISE = (
+MODE_CONV, MODE_STRIDE2, MODE_UP2, MODE_POINTWISE, MODE_STRIDE2_PAD01 = (
     _lib.LDB_CONV_3X3X3,
     _lib.LDB_CONV_3X3X3_S2,
     _lib.LDB_CONV_UP2,
     _lib.LDB_CONV_1X1,
+    _lib.LDB_CONV_3X3X3_S2_PAD01,
 )
 
 
@@ -158,11 +159,14 @@ def _dense_ld(shape, strides, what: str) -> int:
 
 
 def conv_geometry(x_shape, x_strides, packed: PackedWeight, *, stride: int = 1,
-                  in_channels: int | None = None, depth_halo: int = 0) -> tuple[int, tuple[int, int, int], int, int]:
+                  in_channels: int | None = None, depth_halo: int = 0,
+                  pad01: bool = False) -> tuple[int, tuple[int, int, int], int, int]:
     """Validate an NDHWC input layout for ``packed``; return (mode, output grid, x_ld, cin).
 
     With ``depth_halo`` = 1 the first and last depth slices of x are halo
-    slices read by the taps and the output covers the interior slices.
+    slices read by the taps and the output covers the interior slices.  With
+    ``pad01`` a stride-2 conv pads with zeros only after each axis (the VQ
+    encoder's downsample, mlx_model.py:735-736).
     Pure host logic (no device access), shared by ``conv3d_ndhwc`` and the CPU tests.
     """
     x_ld = _dense_ld(x_shape, x_strides, "x")
@@ -183,6 +187,12 @@ def conv_geometry(x_shape, x_strides, packed: PackedWeight, *, stride: int = 1,
         if stride != 1:
             raise ValueError("pointwise convolution has stride 1")
         return MODE_POINTWISE, (depth, height, width), x_ld, cin
+    if stride == 2 and pad01:
+        if min(depth, height, width) < 2:
+            raise ValueError("padding (0, 1) with stride 2 needs extents >= 2")
+        return MODE_STRIDE2_PAD01, tuple((n - 2) // 2 + 1 for n in (depth, height, width)), x_ld, cin
+    if pad01:
+        raise ValueError("pad01 applies to stride-2 convolutions")
     if stride == 2:
         return MODE_STRIDE2, tuple((n - 1) // 2 + 1 for n in (depth, height, width)), x_ld, cin
     if stride != 1:
@@ -205,6 +215,7 @@ def conv3d_ndhwc(
     in_channels: int | None = None,
     stats: torch.Tensor | None = None,
     depth_halo: int = 0,
+    pad01: bool = False,
 ) -> torch.Tensor:
     """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
@@ -224,7 +235,7 @@ def conv3d_ndhwc(
     if x.dtype != torch.float16:
         raise ValueError(f"conv input must be float16 (split planes for FP32), got {x.dtype}")
     mode, grid, x_ld, cin = conv_geometry(tuple(x.shape), tuple(x.stride()), packed, stride=stride,
-                                          in_channels=in_channels, depth_halo=depth_halo)
+                                          in_channels=in_channels, depth_halo=depth_halo, pad01=pad01)
     batch = int(x.shape[0])
     cout = packed.out_channels
     if out_dtype is None:

@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&wmap);
-    const int nmaps = p.mode == kConv3x3x3S2 ? 8 : 1;
+    const int nmaps = (p.mode == kConv3x3x3S2 || p.mode == kConv3x3x3S2Pad01) ? 8 : 1;
     for (int i = 0; i < nmaps; ++i) tma_prefetch_desc(&maps.a[i]);
   }
   if (warp == 2 && lane == 0) {
@@ -745,6 +745,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             x = w0 - (kw == 0);
             y = h0 - (kh == 0);
             z = d0 - (kd == 0);
+          } else if (p.mode == kConv3x3x3S2Pad01) {
+            // input index 2o + k (no padding before): k = 0 -> parity 0 at o,
+            // k = 1 -> parity 1 at o, k = 2 -> parity 0 at o + 1 (past the end:
+            // the zero padding after).
+            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            map = (kd == 1) * 4 + (kh == 1) * 2 + (kw == 1);
+            x = w0 + (kw == 2);
+            y = h0 + (kh == 2);
+            z = d0 + (kd == 2);
           } else if (p.mode == kConvUp2) {
             // parity p, folded tap t reads source index m + p + t - 1.
             const int td = tap >> 2, th = (tap >> 1) & 1, tw = tap & 1;
@@ -1093,7 +1102,7 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   const int B = d->batch, D = d->depth, H = d->height, W = d->width;
   if (B <= 0 || D <= 0 || H <= 0 || W <= 0) return fail(LDB_ERR_SHAPE, "conv input extents must be positive");
   if (d->in_channels <= 0 || d->out_channels <= 0) return fail(LDB_ERR_SHAPE, "conv channels must be positive");
-  if (d->mode < 0 || d->mode > 3) return fail(LDB_ERR_INVALID, "unknown conv mode %d", d->mode);
+  if (d->mode < 0 || d->mode > 4) return fail(LDB_ERR_INVALID, "unknown conv mode %d", d->mode);
   const bool exact = d->exact != 0;
   const int cin = d->in_channels;
   const int cin_pad = ((cin + 15) / 16) * 16;
@@ -1113,7 +1122,8 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   else if (cout <= 128 || exact) bn = 128;
   else bn = 256;
   if (d->depth_halo < 0 || d->depth_halo > 1) return fail(LDB_ERR_SHAPE, "depth_halo must be 0 or 1");
-  if (d->depth_halo && d->mode == LDB_CONV_3X3X3_S2) return fail(LDB_ERR_SHAPE, "depth_halo with stride 2");
+  const bool stride2 = d->mode == LDB_CONV_3X3X3_S2 || d->mode == LDB_CONV_3X3X3_S2_PAD01;
+  if (d->depth_halo && stride2) return fail(LDB_ERR_SHAPE, "depth_halo with stride 2");
   if (D - 2 * d->depth_halo <= 0) return fail(LDB_ERR_SHAPE, "depth %d leaves no interior slice", D);
   ConvParams& p = plan->p;
   p = ConvParams{};
@@ -1125,6 +1135,11 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     gd = (D - 1) / 2 + 1;
     gh = (H - 1) / 2 + 1;
     gw = (W - 1) / 2 + 1;
+  } else if (d->mode == LDB_CONV_3X3X3_S2_PAD01) {
+    if (D < 2 || H < 2 || W < 2) return fail(LDB_ERR_SHAPE, "padding (0, 1) stride 2 needs extents >= 2");
+    gd = (D - 2) / 2 + 1;
+    gh = (H - 2) / 2 + 1;
+    gw = (W - 2) / 2 + 1;
   }
   p.grid_d = gd;
   p.grid_h = gh;
@@ -1261,7 +1276,7 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
   memset(&maps, 0, sizeof(maps));
   const uint32_t abox[5] = {static_cast<uint32_t>(plan.kc), static_cast<uint32_t>(p.bw),
                             static_cast<uint32_t>(p.bh), static_cast<uint32_t>(p.bd), 1u};
-  if (desc->mode == LDB_CONV_3X3X3_S2) {
+  if (desc->mode == LDB_CONV_3X3X3_S2 || desc->mode == LDB_CONV_3X3X3_S2_PAD01) {
     for (int par = 0; par < 8; ++par) {
       const int pd = par >> 2, ph = (par >> 1) & 1, pw = par & 1;
       const uint64_t dims[5] = {cdim, static_cast<uint64_t>((W - pw + 1) / 2), static_cast<uint64_t>((H - ph + 1) / 2),

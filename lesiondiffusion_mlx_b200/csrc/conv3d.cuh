@@ -12,7 +12,8 @@ enum ConvMode : int {
   kConv3x3x3 = 0,    // padding 1, stride 1: 27 taps, rows are output voxels
   kConv3x3x3S2 = 1,  // padding 1, stride 2: 27 taps over 8 parity views of the input
   kConvUp2 = 2,      // conv of a nearest 2x upsampling: 8 parities x 8 folded taps, rows are source voxels
-  kConvPointwise = 3 // 1x1x1 (dense over tokens): one tap
+  kConvPointwise = 3, // 1x1x1 (dense over tokens): one tap
+  kConv3x3x3S2Pad01 = 4 // stride 2, padding 0 before / 1 after: 27 taps over the 8 parity views
 };
 
 enum ConvAct : int { kActNone = 0, kActGelu = 1 };

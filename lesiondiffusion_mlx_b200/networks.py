@@ -134,15 +134,17 @@ class _Layers:
         return t
 
     def conv(self, x: torch.Tensor, key: str, *, stride: int = 1, residual: torch.Tensor | None = None,
-             shift: torch.Tensor | None = None, output_scale: float = 1.0, stats: bool = False) -> torch.Tensor:
+             shift: torch.Tensor | None = None, output_scale: float = 1.0, stats: bool = False,
+             pad01: bool = False) -> torch.Tensor:
         """3x3x3 (stride 1/2, or folded up-2x) or pointwise conv of NDHWC f16 x.
 
         With ``stats`` the output also carries its GroupNorm statistics,
-        accumulated by the conv epilogue, for the GroupNorm that reads it."""
+        accumulated by the conv epilogue, for the GroupNorm that reads it;
+        ``pad01`` pads a stride-2 conv with zeros only after each axis."""
         packed = self.p.conv(key, stride)
         st = self._take_stats(int(x.shape[0]), packed.out_channels) if stats else None
         out = conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
-                           output_scale=output_scale, stats=st)
+                           output_scale=output_scale, stats=st, pad01=pad01)
         if st is not None:
             setattr(out, _GN_STATS, st)
         return out
@@ -428,3 +430,51 @@ class VqDecoderB200(_Layers):
         out = self.norm_silu_conv(x, "decoder.norm_out", "decoder.conv_out", groups=self.groups, eps=eps)
         self._arena = None
         return ops.hu_map(out) if to_hu else out
+
+
+class VqEncoderB200(_Layers):
+    """VQ encoder (mlx_model.py:729-740) on B200 kernels, NDHWC f16.
+
+    conv_in; per level its residual blocks (mlx_model.py:720-727) and, where
+    the weights have one, a stride-2 downsample conv padded with zeros only
+    after each axis (mlx_model.py:735-736); two mid blocks; GroupNorm + SiLU
+    + conv_out; the 1x1 quant_conv.  Levels and blocks follow the weights.
+    """
+
+    def __init__(self, weights: dict[str, torch.Tensor], *, device: torch.device | str = "cuda",
+                 dtype: torch.dtype = torch.float16, groups: int = 16):
+        if dtype != torch.float16:
+            raise ValueError("the B200 encoder runs in float16")
+        super().__init__(_Params(weights, torch.device(device), dtype))
+        self.device = torch.device(device)
+        self.groups = groups
+        names = set(weights)
+        self.levels = sorted({int(m.group(1)) for n in names if (m := re.match(r"encoder\.down\.(\d+)\.", n))})
+        self.blocks = {lvl: sorted({int(m.group(1)) for n in names
+                                    if (m := re.match(rf"encoder\.down\.{lvl}\.block\.(\d+)\.", n))})
+                       for lvl in self.levels}
+        for name in names:
+            if name.startswith(("encoder.", "quant_conv")) and name.endswith(".weight") and weights[name].ndim == 5:
+                key = name[: -len(".weight")]
+                self.p.conv(key, 2 if key.endswith("downsample.conv") else 1)
+
+    def residual(self, x: torch.Tensor, key: str) -> torch.Tensor:
+        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=self.groups, eps=1e-6, stats=True)
+        skip = self.conv(x, key + ".nin_shortcut") if self.p.has(key + ".nin_shortcut.weight") else x
+        return self.norm_silu_conv(h, key + ".norm2", key + ".conv2", groups=self.groups, eps=1e-6, residual=skip,
+                                   stats=True)
+
+    def encode(self, x: torch.Tensor) -> torch.Tensor:
+        """Encode an NDHWC f16 volume (B, D, H, W, C_in) to the latent (B, d, h, w, C_latent)."""
+        self._begin_stats(int(x.shape[0]), x.device)
+        x = self.conv(x, "encoder.conv_in", stats=True)
+        for level in self.levels:
+            for block in self.blocks[level]:
+                x = self.residual(x, f"encoder.down.{level}.block.{block}")
+            if self.p.has(f"encoder.down.{level}.downsample.conv.weight"):
+                x = self.conv(x, f"encoder.down.{level}.downsample.conv", stride=2, pad01=True, stats=True)
+        x = self.residual(x, "encoder.mid.block_1")
+        x = self.residual(x, "encoder.mid.block_2")
+        x = self.norm_silu_conv(x, "encoder.norm_out", "encoder.conv_out", groups=self.groups, eps=1e-6)
+        self._arena = None
+        return self.conv(x, "quant_conv")

@@ -193,6 +193,26 @@ def test_channel_major_tile(cuda_device, shape, out_channels, kind, extra):
     assert np.all(error <= bound), f"max excess {(error - bound).max()}"
 
 
+@pytest.mark.parametrize("shape,out_channels", [((1, 16, 8, 8, 8), 16), ((2, 32, 7, 9, 6), 48),
+                                                ((1, 64, 24, 20, 30), 64)])
+def test_stride2_conv_padded_after_only(cuda_device, shape, out_channels):
+    """Stride 2 with zero padding (0, 1) per axis: the VQ encoder's downsample
+    (mlx_model.py:735-736: pad after, then a stride-2 valid conv)."""
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_weight
+
+    x, w, b = f16_case(shape, out_channels, 3, seed=sum(shape) + 3)
+    out = conv3d_ndhwc(to_ndhwc(x.to(cuda_device), (shape[1] + 7) // 8 * 8), pack_weight(w.to(cuda_device), stride=2),
+                       b.to(cuda_device).float(), stride=2, pad01=True)
+    torch.cuda.synchronize()
+    actual = out.permute(0, 4, 1, 2, 3).double().cpu().numpy()
+    xp = F.pad(x.double(), (0, 1, 0, 1, 0, 1))
+    expected, mag = reference(xp, w.double(), b.double(), 2, 0)
+    assert actual.shape == expected.shape
+    error = np.abs(actual - expected)
+    bound = half_spacing(expected) + ACCUMULATION_EPS * mag
+    assert np.all(error <= bound), f"max excess {(error - bound).max()}"
+
+
 def fp32_case(shape, out_channels, seed):
     rng = np.random.default_rng(seed)
     scales = np.exp(rng.normal(size=(1, shape[1], 1, 1, 1)) * 2)

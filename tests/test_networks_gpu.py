@@ -193,3 +193,20 @@ def test_vq_decoder_matches_reference_recording(cuda_device, quantize):
     oracle = OracleVq(torch_weights(raw, torch.float16))
     ref = oracle.decode(torch.from_numpy(f["z"]).to(torch.float16), quantize=quantize).float().numpy()
     assert rel_l2(got, ref) <= 1e-2
+
+
+def test_vq_encoder_matches_oracle(cuda_device):
+    """VQ encoder (mlx_model.py:729-740), including the stride-2 downsample padded
+    only after each axis, against the oracle on the reference fixture weights."""
+    from lesiondiffusion_mlx_b200.networks import VqEncoderB200
+
+    raw = vq_fixture_weights(7)
+    enc = VqEncoderB200(torch_weights(raw, torch.float16), device=cuda_device)
+    x = np.random.default_rng(4).standard_normal((1, 1, 10, 8, 12)).astype(np.float32)
+    z = enc.encode(to_input(x, cuda_device))
+    torch.cuda.synchronize()
+    got = z.permute(0, 4, 1, 2, 3).float().cpu().numpy()
+    ref = OracleVq(torch_weights(raw, torch.float16)).encode(torch.from_numpy(x).to(torch.float16)).float().numpy()
+    assert got.shape == ref.shape
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) <= 1e-2
