@@ -200,6 +200,18 @@ LDB_API int ldb_flash_attention(ldb_stream_t stream, const void* q, int q_ld, co
                                 int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim,
                                 float scale, int dtype);
 
+/* ldb_flash_attention with a caller workspace that lets the kernel split the
+ * keys over several CTAs when (query pairs x heads x batch) would leave SMs
+ * idle: each split writes its unnormalised O rows and (max, sum) to the
+ * workspace and a second kernel merges them (the online-softmax merge of
+ * _attention_half.py:58-113 across key ranges).  With a null or too small
+ * workspace it runs unsplit.  Workspace bytes from
+ * ldb_flash_attention_workspace_size (0: no split would help). */
+LDB_API int ldb_flash_attention_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes);
+LDB_API int ldb_flash_attention_ws(ldb_stream_t stream, const void* q, int q_ld, const void* k, const void* v,
+                                   int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads,
+                                   int head_dim, float scale, int dtype, void* workspace, size_t workspace_bytes);
+
 /* -------------------------------------------------------------------------
  * Denoise-loop kernels.
  * ---------------------------------------------------------------------- */

@@ -210,3 +210,25 @@ def test_vq_encoder_matches_oracle(cuda_device):
     assert got.shape == ref.shape
     assert np.all(np.isfinite(got))
     assert rel_l2(got, ref) <= 1e-2
+
+
+def test_bundle_loaders_build_the_same_networks(cuda_device, tmp_path):
+    """Networks built from the stage-prefixed safetensors bundle (medmlx.py:1585-1602)
+    decode and encode like networks built from the same state dict cast to f16
+    (the stage loader casts every array, as the reference's does); GroupNorm
+    statistics are summed with atomics, so runs agree to rounding, not bits."""
+    from lesiondiffusion_mlx_b200.networks import VqDecoderB200, VqEncoderB200
+    from lesiondiffusion_mlx_b200.weights import load_vq_decoder, load_vq_encoder, write_safetensors
+
+    raw = vq_fixture_weights(7)
+    write_safetensors(tmp_path / "model.safetensors", {"vq." + k: v for k, v in raw.items()})
+    tw = {k: torch.from_numpy(np.asarray(v)).to(torch.float16) for k, v in raw.items()}
+    z = to_input(np.random.default_rng(2).standard_normal((1, 4, 3, 4, 5)).astype(np.float32), cuda_device)
+    a = VqDecoderB200({k: v for k, v in tw.items() if not k.startswith("encoder")}, device=cuda_device).decode(z)
+    b = load_vq_decoder(tmp_path, device=cuda_device).decode(z)
+    x = to_input(np.random.default_rng(3).standard_normal((1, 1, 6, 8, 8)).astype(np.float32), cuda_device)
+    c = VqEncoderB200(tw, device=cuda_device).encode(x)
+    d = load_vq_encoder(tmp_path, device=cuda_device).encode(x)
+    torch.cuda.synchronize()
+    assert rel_l2(a.float().cpu().numpy(), b.float().cpu().numpy()) <= 2e-3
+    assert rel_l2(c.float().cpu().numpy(), d.float().cpu().numpy()) <= 2e-3
