@@ -373,8 +373,8 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
     const unsigned int valid = __ballot_sync(0xffffffffu, row_voxel(p, c, st.row) >= 0);
     if ((st.row & 31) == 0) vmask[st.quarter] = valid;
   }
-  bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
-  tc_fence_after();
+  // bias + shift of the tile's columns, read while the MMAs still run (the
+  // previous run's statistics were flushed above with its own values)
   if (!SPLIT) {
     for (int j = et; j < BN; j += 128) {
       const int col = n0 + j;
@@ -386,6 +386,8 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
       st.bsum[j] = add;
     }
   }
+  bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
+  tc_fence_after();
   named_barrier(1, 128);
   if (!SPLIT && p.stats)  // every thread counts the tile's valid rows (the masks are visible after the barrier)
     st.run_rows += static_cast<int>(__popc(vmask[0]) + __popc(vmask[1]) + __popc(vmask[2]) + __popc(vmask[3]));
@@ -444,46 +446,53 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
         st.rq += 1;
         rbuf = res_base + rb * Cfg::kEpiBufBytes;
       }
+      // Every shared-memory read of the chunk (bias + shift, the residual)
+      // comes before its first staging store: the compiler cannot tell the
+      // staging buffer from those arrays, and loads interleaved with stores
+      // would run one after another.
 #pragma unroll
-      for (int u = 0; u < CC / kPerUnit; ++u) {
-        const uint32_t off = swizzle_offset(rowoff + u * 16, kRowBytes);
-        float y[kPerUnit];
+      for (int j = 0; j < CC; ++j) v[j] = (v[j] + st.bsum[c0 + j]) * p.out_scale;
+      if (rbuf) {
 #pragma unroll
-        for (int j = 0; j < kPerUnit; ++j) y[j] = (v[u * kPerUnit + j] + st.bsum[c0 + u * kPerUnit + j]) * p.out_scale;
-        if (rbuf) {
+        for (int u = 0; u < CC / kPerUnit; ++u) {
+          const uint32_t off = swizzle_offset(rowoff + u * 16, kRowBytes);
           if constexpr (EXACT) {
             const float4 rr = *reinterpret_cast<const float4*>(rbuf + off);
-            y[0] += rr.x;
-            y[1] += rr.y;
-            y[2] += rr.z;
-            y[3] += rr.w;
+            v[4 * u] += rr.x;
+            v[4 * u + 1] += rr.y;
+            v[4 * u + 2] += rr.z;
+            v[4 * u + 3] += rr.w;
           } else {
             const uint4 raw = *reinterpret_cast<const uint4*>(rbuf + off);
             const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float2 f = __half22float2(h2[j]);
-              y[2 * j] += f.x;
-              y[2 * j + 1] += f.y;
+              v[8 * u + 2 * j] += f.x;
+              v[8 * u + 2 * j + 1] += f.y;
             }
           }
         }
-        if (p.act == kActGelu) {
+      }
+      if (p.act == kActGelu) {
 #pragma unroll
-          for (int j = 0; j < kPerUnit; ++j) {
-            // The reference rounds the dense output to the activation dtype
-            // before its FP32 GELU (mlx_model.py:369-374 after :204-217).
-            const float z = EXACT ? y[j] : __half2float(__float2half_rn(y[j]));
-            y[j] = gelu_erf_f32(z);
-          }
+        for (int j = 0; j < CC; ++j) {
+          // The reference rounds the dense output to the activation dtype
+          // before its FP32 GELU (mlx_model.py:369-374 after :204-217).
+          const float z = EXACT ? v[j] : __half2float(__float2half_rn(v[j]));
+          v[j] = gelu_erf_f32(z);
         }
+      }
+#pragma unroll
+      for (int u = 0; u < CC / kPerUnit; ++u) {
+        const uint32_t off = swizzle_offset(rowoff + u * 16, kRowBytes);
         if constexpr (EXACT) {
-          *reinterpret_cast<float4*>(ob + off) = make_float4(y[0], y[1], y[2], y[3]);
+          *reinterpret_cast<float4*>(ob + off) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
         } else {
           uint4 raw;
           __half2* h2 = reinterpret_cast<__half2*>(&raw);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+          for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(v[8 * u + 2 * j], v[8 * u + 2 * j + 1]);
           *reinterpret_cast<uint4*>(ob + off) = raw;
         }
       }
@@ -609,10 +618,17 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
     const bool dvalid = d0 + pl < p.grid_d;
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = (v[j] + add) * p.out_scale;
+    if (rbuf) {  // all residual reads before the first staging store (see epilogue_tile)
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        v[j] += __half2float(*reinterpret_cast<const __half*>(
+            rbuf + box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128)));
+    }
+#pragma unroll
     for (int j = 0; j < 64; ++j) {
       const uint32_t off = box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128);
-      float y = (v[j] + add) * p.out_scale;
-      if (rbuf) y += __half2float(*reinterpret_cast<const __half*>(rbuf + off));
+      float y = v[j];
       if (p.act == kActGelu) y = gelu_erf_f32(__half2float(__float2half_rn(y)));
       const __half h = __float2half_rn(y);
       if (live) *reinterpret_cast<__half*>(ob + off) = h;
