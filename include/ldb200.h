@@ -185,6 +185,22 @@ LDB_API int ldb_group_norm_affine_from_stats(ldb_stream_t stream, const double* 
                                              const double* stats2, int c2, int batch, int voxels, int groups,
                                              const float* gamma, const float* beta, float eps, float* affine);
 
+/* ldb_group_norm_affine_from_stats followed by ldb_prepare_input in one
+ * launch: each block derives the affine of its batch item from the producer
+ * statistics (the same values, bit for bit) into shared memory and applies it
+ * with SiLU and the f16 rounding or FP32 hi/lo split.  `voxels` per batch
+ * item are normalized; `stat_voxels` is the voxel count the statistics cover
+ * (0: the same; larger when x is one slab of a volume whose statistics were
+ * summed over all slabs).  Replaces the
+ * reference's group_norm_affine + conv-prologue pair of a norm_silu_conv
+ * (lesiondiffusion_mlx/mlx_model.py:328-342) when the producing convs
+ * accumulated statistics. */
+LDB_API int ldb_prepare_input_from_stats(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2,
+                                         int c2, int ld2, int dtype, int batch, int voxels, int stat_voxels,
+                                         const double* stats1,
+                                         const double* stats2, int groups, const float* gamma, const float* beta,
+                                         float eps, int silu, int split, void* out, int out_ld);
+
 /* LayerNorm over the last axis of f16 rows (mlx_model.py:360-367). */
 LDB_API int ldb_layer_norm(ldb_stream_t stream, const void* x, int x_ld, const float* gamma, const float* beta,
                            float eps, void* out, int out_ld, int rows, int channels);

@@ -70,6 +70,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_group_norm_affine_noalloc": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P],
     "ldb_prepare_input": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I],
     "ldb_group_norm_affine_from_stats": [_P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _F, _P],
+    "ldb_prepare_input_from_stats": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _F, _I, _I, _P, _I],
     "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
     "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],
     "ldb_flash_attention_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],

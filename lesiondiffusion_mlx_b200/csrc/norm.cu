@@ -214,20 +214,15 @@ __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, i
   }
 }
 
-// out = prepare(x): optional affine (B, C, 2) and SiLU in FP32, then either
-// one f16 rounding or the exact split into hi / 2^11-scaled lo planes
-// (_nax_conv.py:109-155).  Channels past C up to the padded plane width are
-// written as zeros.  One thread per 8 channels of one voxel.
-__global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_batch, const float* affine, int silu,
-                               int split, int cpad, __half* out, int out_ld) {
-  pdl_begin();
+// out = prepare(x): optional affine (scale, offset per channel) and SiLU in
+// FP32, then either one f16 rounding or the exact split into hi / 2^11-scaled
+// lo planes (_nax_conv.py:109-155).  Channels past C up to the padded plane
+// width are written as zeros.  One call per 8 channels of one voxel; `aff`
+// points at the (scale, offset) pairs of channels c .. c + 7 (global or
+// shared memory) or is null.
+__device__ __forceinline__ void prepare_vec(const Src2& s, long long voxel, int c, const float* aff, int silu,
+                                            int split, int cpad, __half* out, int out_ld) {
   const int c_total = s.c1 + s.c2;
-  const int vecs = cpad / 8;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= voxels_total * vecs) return;
-  const long long voxel = idx / vecs;
-  const int c = static_cast<int>(idx % vecs) * 8;
-  const int b = static_cast<int>(voxel / voxels_per_batch);
   float v[8];
   if (c + 8 <= c_total) {
     load8(s, voxel, c, v);
@@ -239,9 +234,10 @@ __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_ba
   __half* hi = reinterpret_cast<__half*>(&hi_raw);
   __half* lo = reinterpret_cast<__half*>(&lo_raw);
   float sc[8], of[8];
-  if (affine && c + 8 <= c_total) {
+  const bool affine = aff != nullptr && c + 8 <= c_total;
+  if (affine) {
     // 8 (scale, offset) pairs = four 16-byte loads
-    const float4* a4 = reinterpret_cast<const float4*>(affine + (static_cast<long long>(b) * c_total + c) * 2);
+    const float4* a4 = reinterpret_cast<const float4*>(aff);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float4 t = a4[q];
@@ -267,45 +263,121 @@ __global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_ba
   if (split) *reinterpret_cast<uint4*>(o + cpad) = lo_raw;
 }
 
-// GroupNorm affine from producer statistics: per (batch, channel) FP64 sum
-// and sum of squares of each source block, as the convolution epilogue adds
-// them up.  One warp per (group, batch): lanes stride over the group's
-// channels, a shuffle tree gives every lane the totals, and each lane writes
-// (scale, offset) of its channels with the same arithmetic as
-// gn_finalize_kernel (biased variance over the group's channels and voxels).
+// One thread per 8 channels of one voxel; `affine` is (B, C, 2) or null.
+__global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_batch, const float* affine, int silu,
+                               int split, int cpad, __half* out, int out_ld) {
+  pdl_begin();
+  const int c_total = s.c1 + s.c2;
+  const int vecs = cpad / 8;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= voxels_total * vecs) return;
+  const long long voxel = idx / vecs;
+  const int c = static_cast<int>(idx % vecs) * 8;
+  const int b = static_cast<int>(voxel / voxels_per_batch);
+  const float* aff = affine ? affine + (static_cast<long long>(b) * c_total + c) * 2 : nullptr;
+  prepare_vec(s, voxel, c, aff, silu, split, cpad, out, out_ld);
+}
+
+// GroupNorm affine of batch item b from producer statistics (per channel FP64
+// sum and sum of squares of each source block, as the convolution epilogue
+// adds them up), computed by one thread block in shared memory.  The caller
+// has staged gamma / beta in aff[2c], aff[2c + 1] (before its dependency
+// wait: they are weights, not the previous kernel's output); this loads the
+// statistics with one coalesced sweep, sums each group in channel order on
+// one thread (biased variance over the group's channels and voxels, as
+// gn_finalize_kernel), and overwrites aff with (scale, offset).  Ends with a
+// barrier.  sts holds 2 C doubles, gm 2 * groups doubles.
+__device__ __forceinline__ void block_affine_from_stats(const double* st1, int c1, const double* st2, int c2, int b,
+                                                        int groups, int voxels, float eps, float* aff, double* sts,
+                                                        double* gm) {
+  const int C = c1 + c2;
+  const int cpg = C / groups;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const double* src = c < c1 ? st1 + (static_cast<long long>(b) * c1 + c) * 2
+                               : st2 + (static_cast<long long>(b) * c2 + (c - c1)) * 2;
+    const double2 v = *reinterpret_cast<const double2*>(src);
+    sts[2 * c] = v.x;
+    sts[2 * c + 1] = v.y;
+  }
+  __syncthreads();
+  const double inv_n = 1.0 / (static_cast<double>(voxels) * cpg);
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    double a = 0.0, q = 0.0;
+    for (int c = g * cpg; c < (g + 1) * cpg; ++c) {
+      a += sts[2 * c];
+      q += sts[2 * c + 1];
+    }
+    const double mean = a * inv_n;
+    const double var = fmax(q * inv_n - mean * mean, 0.0);
+    gm[2 * g] = mean;
+    gm[2 * g + 1] = 1.0 / sqrt(var + static_cast<double>(eps));
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const int g = c / cpg;
+    const double mean = gm[2 * g], rstd = gm[2 * g + 1];
+    const float scale = static_cast<float>(static_cast<double>(aff[2 * c]) * rstd);
+    const float offset = static_cast<float>(static_cast<double>(aff[2 * c + 1]) - mean * static_cast<double>(scale));
+    aff[2 * c] = scale;
+    aff[2 * c + 1] = offset;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void stage_gamma_beta(const float* gamma, const float* beta, int C, float* aff) {
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    aff[2 * c] = gamma ? gamma[c] : 1.f;
+    aff[2 * c + 1] = beta ? beta[c] : 0.f;
+  }
+}
+
+// Shared memory of the two kernels below: aff [C][2] f32, sts [C][2] f64,
+// gm [groups][2] f64.
+inline size_t stats_smem_bytes(int C, int groups) {
+  return static_cast<size_t>(C) * 2 * sizeof(double) + static_cast<size_t>(groups) * 2 * sizeof(double) +
+         static_cast<size_t>(C) * 2 * sizeof(float);
+}
+
+// The affine alone: one block per batch item into (B, C, 2).
 __global__ void gn_stats_affine_kernel(const double* st1, int c1, const double* st2, int c2, int voxels,
                                        int groups, const float* gamma, const float* beta, float eps,
                                        float* affine) {
-  pdl_begin();
+  extern __shared__ double2 smem2[];
   const int C = c1 + c2;
-  const int cpg = C / groups;
+  double* sts = reinterpret_cast<double*>(smem2);
+  double* gm = sts + 2 * C;
+  float* aff = reinterpret_cast<float*>(gm + 2 * groups);
+  const int b = blockIdx.x;
+  stage_gamma_beta(gamma, beta, C, aff);
+  pdl_begin();
+  block_affine_from_stats(st1, c1, st2, c2, b, groups, voxels, eps, aff, sts, gm);
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) affine[static_cast<long long>(b) * C * 2 + i] = aff[i];
+}
+
+// GroupNorm from producer statistics fused with the normalize pass: block
+// (x, b) derives the affine of batch item b into shared memory (the same
+// arithmetic as gn_stats_affine_kernel, so the same bits), then applies it
+// with prepare_vec over a grid-stride range of b's voxels.
+__global__ void prepare_stats_kernel(Src2 s, int voxels, int stat_voxels, const double* st1, const double* st2,
+                                     int groups, const float* gamma, const float* beta, float eps, int silu,
+                                     int split, int cpad, __half* out, int out_ld) {
+  extern __shared__ double2 smem2[];
+  const int C = s.c1 + s.c2;
+  double* sts = reinterpret_cast<double*>(smem2);
+  double* gm = sts + 2 * C;
+  float* aff = reinterpret_cast<float*>(gm + 2 * groups);
   const int b = blockIdx.y;
-  const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (g >= groups) return;
-  double a = 0.0, q = 0.0;
-  for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
-    const double* src = c < c1 ? st1 + (static_cast<long long>(b) * c1 + c) * 2
-                               : st2 + (static_cast<long long>(b) * c2 + (c - c1)) * 2;
-    a += src[0];
-    q += src[1];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    q += __shfl_xor_sync(0xffffffffu, q, o);
-  }
-  const double inv_n = 1.0 / (static_cast<double>(voxels) * cpg);
-  const double mean = a * inv_n;
-  const double var = fmax(q * inv_n - mean * mean, 0.0);
-  const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
-  for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
-    const float gam = gamma ? gamma[c] : 1.f;
-    const float bet = beta ? beta[c] : 0.f;
-    const float scale = static_cast<float>(static_cast<double>(gam) * rstd);
-    const float offset = static_cast<float>(static_cast<double>(bet) - mean * static_cast<double>(scale));
-    affine[(static_cast<long long>(b) * C + c) * 2] = scale;
-    affine[(static_cast<long long>(b) * C + c) * 2 + 1] = offset;
+  stage_gamma_beta(gamma, beta, C, aff);
+  pdl_begin();
+  block_affine_from_stats(st1, s.c1, st2, s.c2, b, groups, stat_voxels, eps, aff, sts, gm);
+  const int vecs = cpad / 8;
+  const long long total = static_cast<long long>(voxels) * vecs;
+  const long long v0 = static_cast<long long>(b) * voxels;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long vox = idx / vecs;
+    const int c = static_cast<int>(idx - vox * vecs) * 8;
+    prepare_vec(s, v0 + vox, c, c < C ? aff + c * 2 : nullptr, silu, split, cpad, out, out_ld);
   }
 }
 
@@ -390,6 +462,13 @@ int make_src(const void* x1, int c1, int ld1, const void* x2, int c2, int ld2, i
   s->ld2 = c2 > 0 ? ld2 : ld1;
   s->f32 = dtype == LDB_F32;
   return LDB_OK;
+}
+
+// Kernels whose shared memory grows with the channel count may need more
+// than the default 48 KB (at most 4096 channels: 97 KB plus the groups).
+int stats_smem_attribute(const void* kernel, size_t bytes, unsigned long long* configured) {
+  if (bytes <= 48 * 1024) return LDB_OK;
+  return ensure_smem_attribute(kernel, 100 * 1024, configured, "stats smem attribute");
 }
 
 int gn_chunks(int voxels, int batch) {
@@ -512,10 +591,44 @@ int ldb_group_norm_affine_from_stats(cudaStream_t stream, const double* stats1, 
   if (c1 <= 0 || c2 < 0 || batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "extents must be positive");
   const int C = c1 + c2;
   if (groups <= 0 || C % groups) return fail(LDB_ERR_SHAPE, "groups %d must divide channels %d", groups, C);
+  if (C > 4096) return fail(LDB_ERR_SHAPE, "at most 4096 channels");
+  const size_t smem = stats_smem_bytes(C, groups);
+  static unsigned long long configured = 0;
+  int rc = stats_smem_attribute(reinterpret_cast<const void*>(gn_stats_affine_kernel), smem, &configured);
+  if (rc != LDB_OK) return rc;
+  return launch_kernel(gn_stats_affine_kernel, dim3(batch), dim3(256), smem, stream, "gn affine from stats launch",
+                       stats1, c1, c2 > 0 ? stats2 : stats1, c2, voxels, groups, gamma, beta, eps, affine);
+}
+
+int ldb_prepare_input_from_stats(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
+                                 int ld2, int dtype, int batch, int voxels, int stat_voxels, const double* stats1,
+                                 const double* stats2, int groups, const float* gamma, const float* beta, float eps,
+                                 int silu, int split, void* out, int out_ld) {
+  using namespace ldb;
+  Src2 s;
+  int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
+  if (rc != LDB_OK) return rc;
+  if (!out || !stats1 || (s.c2 > 0 && !stats2)) return fail(LDB_ERR_INVALID, "prepare from stats: null pointer");
+  if (batch <= 0 || voxels <= 0 || stat_voxels < 0) return fail(LDB_ERR_SHAPE, "extents must be positive");
+  if (stat_voxels == 0) stat_voxels = voxels;
+  const int C = s.c1 + s.c2;
+  if (groups <= 0 || C % groups) return fail(LDB_ERR_SHAPE, "groups %d must divide channels %d", groups, C);
+  if (C > 4096) return fail(LDB_ERR_SHAPE, "at most 4096 channels");
+  const int cpad = split ? ((C + 15) / 16) * 16 : ((C + 7) / 8) * 8;
+  if (out_ld % 8 || out_ld < (split ? 2 * cpad : cpad))
+    return fail(LDB_ERR_ALIGNMENT, "out_ld %d too small or not a multiple of 8", out_ld);
+  const size_t smem = stats_smem_bytes(C, groups);
+  static unsigned long long configured = 0;
+  rc = stats_smem_attribute(reinterpret_cast<const void*>(prepare_stats_kernel), smem, &configured);
+  if (rc != LDB_OK) return rc;
   const int threads = 256;
-  return launch_kernel(gn_stats_affine_kernel, dim3((groups * 32 + threads - 1) / threads, batch), dim3(threads), 0,
-                       stream, "gn affine from stats launch", stats1, c1, c2 > 0 ? stats2 : stats1, c2, voxels,
-                       groups, gamma, beta, eps, affine);
+  const long long per_batch = static_cast<long long>(voxels) * (cpad / 8);
+  // About 8 blocks of 256 threads per SM over the whole batch.
+  const long long cap = std::max(1, (8 * sm_count()) / batch);
+  const long long blocks = std::min((per_batch + threads - 1) / threads, cap);
+  return launch_kernel(prepare_stats_kernel, dim3(static_cast<unsigned>(blocks), batch), dim3(threads), smem,
+                       stream, "prepare from stats launch", s, voxels, stat_voxels, stats1, s.c2 > 0 ? stats2 : stats1, groups,
+                       gamma, beta, eps, silu, split, cpad, static_cast<__half*>(out), out_ld);
 }
 
 int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,

@@ -151,18 +151,16 @@ class _Layers:
 
     def group_norm_input(self, x: torch.Tensor, norm_key: str, *, groups: int, eps: float, silu: bool,
                          x2: torch.Tensor | None = None) -> torch.Tensor:
-        """``f16(silu?(GN([x | x2])))``: the affine from the producers' statistics
-        when both sources carry them, else from a statistics pass; then the
-        normalize pass."""
+        """``f16(silu?(GN([x | x2])))``: one normalize pass that derives the affine
+        from the producers' statistics when both sources carry them, else a
+        statistics pass and then the normalize pass."""
         gamma, beta = self.p.f32(norm_key + ".weight"), self.p.f32(norm_key + ".bias")
         st1 = getattr(x, _GN_STATS, None)
         st2 = None if x2 is None else getattr(x2, _GN_STATS, None)
         if st1 is not None and (x2 is None or st2 is not None):
-            voxels = int(x.shape[1]) * int(x.shape[2]) * int(x.shape[3])
-            affine = ops.group_norm_affine_from_stats(st1, gamma, beta, voxels=voxels, groups=groups, eps=eps,
-                                                      stats2=st2)
-        else:
-            affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=eps, x2=x2)
+            return ops.prepare_input_from_stats(x, st1, gamma, beta, groups=groups, eps=eps, silu=silu, x2=x2,
+                                                stats2=st2)
+        affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=eps, x2=x2)
         return ops.prepare_input(x, affine=affine, silu=silu, x2=x2)
 
     def norm_silu_conv(self, x: torch.Tensor, norm_key: str, conv_key: str, *, groups: int, eps: float,

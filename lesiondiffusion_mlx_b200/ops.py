@@ -126,6 +126,42 @@ def group_norm_affine_from_stats(
     return affine
 
 
+def prepare_input_from_stats(
+    x: torch.Tensor, stats: torch.Tensor, gamma: torch.Tensor | None, beta: torch.Tensor | None, *, groups: int,
+    eps: float, silu: bool = False, split: bool = False, x2: torch.Tensor | None = None,
+    stats2: torch.Tensor | None = None, out: torch.Tensor | None = None, voxels: int | None = None,
+) -> torch.Tensor:
+    """``prepare_input(x, affine=group_norm_affine_from_stats(stats, ...))`` in
+    one launch.  ``voxels`` is the count per batch item the statistics cover
+    (default: those of ``x``; larger for one slab of a sharded volume)."""
+    per_batch, c1, ld1 = _rows(x)
+    batch = int(x.shape[0])
+    c2, ld2 = 0, 0
+    if x2 is not None:
+        _, c2, ld2 = _rows(x2)
+    for s, c in ((stats, c1), (stats2, c2)):
+        if s is None and c == 0:
+            continue
+        if (s is None or s.dtype != torch.float64 or tuple(s.shape) != (batch, c, 2) or not s.is_contiguous()):
+            raise ValueError(f"stats must be contiguous float64 {(batch, c, 2)} tensors, one per source")
+    channels = c1 + c2
+    cpad = (channels + 15) // 16 * 16 if split else (channels + 7) // 8 * 8
+    width = 2 * cpad if split else cpad
+    lead = tuple(int(s) for s in x.shape[:-1])
+    if out is None:
+        out = torch.empty((*lead, width), dtype=torch.float16, device=x.device)
+    _, _, out_ld = _rows(out)
+    g = None if gamma is None else gamma.to(torch.float32).contiguous()
+    b = None if beta is None else beta.to(torch.float32).contiguous()
+    with instrument.maybe_time("prepare", 0.0):
+        _lib.call(
+            "ldb_prepare_input_from_stats", _stream(x), x.data_ptr(), c1, ld1, _ptr(x2), c2, ld2, _DT[x.dtype],
+            batch, per_batch, int(voxels or 0), stats.data_ptr(), _ptr(stats2), groups, _ptr(g), _ptr(b), float(eps), int(silu),
+            int(split), out.data_ptr(), out_ld,
+        )
+    return out if split else out[..., :channels]
+
+
 def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """Last-axis LayerNorm of f16 rows; ``gamma``/``beta`` f32."""

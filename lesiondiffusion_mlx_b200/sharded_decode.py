@@ -167,9 +167,8 @@ class ShardedVqDecoder:
         gamma, beta = self.p.f32(key + ".weight"), self.p.f32(key + ".bias")
         out = self._new(src, src[0].channels)
         for s, o in zip(src, out):
-            affine = ops.group_norm_affine_from_stats(s.stats, gamma, beta, voxels=voxels, groups=self.dec.groups,
-                                                      eps=eps)
-            ops.prepare_input(s.x, affine=affine, silu=True, out=o.x)
+            ops.prepare_input_from_stats(s.x, s.stats, gamma, beta, groups=self.dec.groups, eps=eps, silu=True,
+                                         out=o.x, voxels=voxels)
         return out
 
     def _residual(self, x: list[_Slab], key: str, voxels: int, scaled_in: bool, scaled_out: bool) -> list[_Slab]:

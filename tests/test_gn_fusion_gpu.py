@@ -117,6 +117,46 @@ def test_affine_from_stats_matches_oracle_group_norm(cuda_device, dtype, shape, 
     assert np.all(np.abs(got.numpy() - want.numpy()) <= 2 * ulp + 1e-6)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("shape,groups,split,exact", [((2, 64, 3, 5, 7), 32, None, False),
+                                                      ((1, 768, 2, 4, 5), 32, 512, False),
+                                                      ((3, 96, 3, 4, 5), 32, 40, True),
+                                                      ((1, 128, 8, 9, 10), 16, None, True)])
+def test_prepare_from_stats_equals_affine_then_prepare(cuda_device, dtype, shape, groups, split, exact):
+    """The one-launch normalize pass gives the same bits as the affine kernel
+    followed by the plain normalize pass (both sources, f16 rounding and the
+    FP32 hi/lo split, several batch items)."""
+    from lesiondiffusion_mlx_b200 import ops
+
+    rng = np.random.default_rng(sum(shape) + 11)
+    x = torch.from_numpy((rng.normal(size=shape) * 2 - 0.7).astype(np.float32)).to(dtype)
+    gamma = torch.from_numpy(rng.normal(size=shape[1]).astype(np.float32)).to(cuda_device)
+    beta = torch.from_numpy(rng.normal(size=shape[1]).astype(np.float32)).to(cuda_device)
+    xd = ndhwc(x).to(cuda_device)
+    voxels = shape[2] * shape[3] * shape[4]
+
+    def sums(t: torch.Tensor) -> torch.Tensor:
+        v = t.double().reshape(t.shape[0], -1, t.shape[-1])
+        return torch.stack([v.sum(1), (v * v).sum(1)], dim=-1).contiguous()
+
+    x1, x2 = (xd[..., :split].contiguous(), xd[..., split:].contiguous()) if split else (xd, None)
+    s1, s2 = sums(x1), (None if x2 is None else sums(x2))
+    affine = ops.group_norm_affine_from_stats(s1, gamma, beta, voxels=voxels, groups=groups, eps=1e-5, stats2=s2)
+    want = ops.prepare_input(x1, affine=affine, silu=True, split=exact, x2=x2)
+    got = ops.prepare_input_from_stats(x1, s1, gamma, beta, groups=groups, eps=1e-5, silu=True, split=exact, x2=x2,
+                                       stats2=s2)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    # statistics of a larger volume (one slab of a sharded decode): the voxel count is the volume's
+    affine = ops.group_norm_affine_from_stats(s1, gamma, beta, voxels=3 * voxels, groups=groups, eps=1e-5,
+                                              stats2=s2)
+    want = ops.prepare_input(x1, affine=affine, silu=True, split=exact, x2=x2)
+    got = ops.prepare_input_from_stats(x1, s1, gamma, beta, groups=groups, eps=1e-5, silu=True, split=exact, x2=x2,
+                                       stats2=s2, voxels=3 * voxels)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
 def test_fused_statistics_feed_group_norm(cuda_device):
     """conv (with statistics) -> affine from statistics equals the statistics
     pass over the same conv output."""
