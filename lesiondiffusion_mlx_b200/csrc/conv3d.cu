@@ -716,7 +716,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_begin();
+  // Programmatic dependent launch: the next kernel may be scheduled at once;
+  // each thread that touches global memory the previous kernel may write
+  // waits for it first.  The producer waits only right before its first TMA
+  // load, so its first tile's arithmetic (and the instruction fetch of that
+  // code) overlaps the previous kernel's tail; the MMA warp reads only shared
+  // memory and TMEM and never waits.
+  pdl_trigger();
 
   const uint32_t a_box_bytes = static_cast<uint32_t>(KC * 2 * p.bw * p.bh * p.bd);
   const uint32_t tx_bytes = Cfg::kPlanes * (a_box_bytes + static_cast<uint32_t>(Cfg::kBBytesRaw));
@@ -727,6 +733,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_parity = 0;
+      bool waited = false;
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord c = decode_tile(p, t);
         const int kb0 = c.ks * p.kb_per_split;
@@ -778,6 +785,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             z = d0 + pd + td - 1;
           }
           z += p.in_zoff;
+          if (!waited) {
+            pdl_wait();
+            waited = true;
+          }
           tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
           tma_load_2d(sb, &wmap, &full[stage], tap * p.cin_pad + chn, brow);
           if (EXACT) {
@@ -863,6 +874,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();
     EpiState st;
     st.epi = epi;
     st.res_full = res_full;
