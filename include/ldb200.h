@@ -283,6 +283,35 @@ LDB_API int ldb_resize_nearest(ldb_stream_t stream, const void* x, int batch, in
  * mlx_pipeline.py:72-96). */
 LDB_API int ldb_hu_map(ldb_stream_t stream, const void* x, int dtype, int x_ld, long long n, float* out);
 
+/* -------------------------------------------------------------------------
+ * Output-region compositing of a generated CT into the input CT
+ * (localize_output and apply_lesion_change, medmlx.py:2531-2690).  Volumes
+ * are dense float32 (n0, n1, n2) arrays in the reference's axis order.
+ * ---------------------------------------------------------------------- */
+
+/* output_region = "box": out = generated inside the box [start, stop) (host
+ * arrays of 3), w * generated + (1 - w) * original within margin_mm of it
+ * (w = 0.5 (1 + cos(pi d / margin)), d the Euclidean distance in mm between
+ * voxel centres with per-axis spacing spacing_mm[3]), original elsewhere.
+ * weighted_count (device, optional) gets the number of voxels with
+ * d < margin added to it. */
+LDB_API int ldb_localize_box(ldb_stream_t stream, const float* original, const float* generated, float* out, int n0,
+                             int n1, int n2, const int* start, const int* stop, const double* spacing_mm,
+                             double margin_mm, unsigned long long* weighted_count);
+
+/* Lesion extent of a uint8 mask: extent[7] (device) = voxel count, minimum
+ * index per axis, maximum index per axis. */
+LDB_API int ldb_lesion_extent(ldb_stream_t stream, const uint8_t* lesion, int n0, int n1, int n2, int* extent);
+
+/* output_region = "lesion": out = original + (generated - reconstruction)
+ * within `reach` voxels of a lesion voxel along every axis, original
+ * elsewhere (f32 arithmetic).  stats[3] (device) = the sum and count of
+ * reconstruction - original over the reached non-lesion voxels with
+ * |original| < 1000, and the reached count.  workspace >= 2 n0 n1 n2 bytes. */
+LDB_API int ldb_apply_lesion_change(ldb_stream_t stream, const float* original, const float* generated,
+                                    const float* reconstruction, const uint8_t* lesion, float* out, int n0, int n1,
+                                    int n2, int reach, uint8_t* workspace, size_t workspace_bytes, double* stats);
+
 #ifdef __cplusplus
 }
 #endif

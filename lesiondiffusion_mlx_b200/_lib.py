@@ -81,6 +81,9 @@ SIGNATURES: dict[str, list] = {
     "ldb_sampler_step": [_P, _I, _P, _P, _P, _I, _P, ctypes.c_longlong, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P],
     "ldb_vq_nearest4": [_P, _P, _I, ctypes.c_longlong, _P, _I, _I, _P, _P, _I],
     "ldb_resize_nearest": [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _I, _I],
+    "ldb_localize_box": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, ctypes.c_double, _P],
+    "ldb_lesion_extent": [_P, _P, _I, _I, _I, _P],
+    "ldb_apply_lesion_change": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P],
     "ldb_hu_map": [_P, _P, _I, _I, ctypes.c_longlong, _P],
 }
 _RESTYPES = {"ldb_last_error": ctypes.c_char_p, "ldb_launch_count": ctypes.c_ulonglong}
