@@ -223,6 +223,20 @@ LDB_API int ldb_flash_attention(ldb_stream_t stream, const void* q, int q_ld, co
  * _attention_half.py:58-113 across key ranges).  With a null or too small
  * workspace it runs unsplit.  Workspace bytes from
  * ldb_flash_attention_workspace_size (0: no split would help). */
+/* FP32 attention for 32-wide heads (the reference's FP32 flash_attention,
+ * _attention.py:148-375): q, k, v, out are f32 projections (B, L, H*32) with
+ * row strides q_ld / kv_ld / out_ld (multiples of 4, 16-byte aligned
+ * pointers).  Runs the tcgen05 kernel in split-f16 form: Q * scale * log2(e),
+ * K and V become f16 hi / low planes in `workspace`
+ * (ldb_flash_attention_f32_workspace_size bytes); scores Qh Kh + Qh Kl + Ql Kh
+ * and probabilities split the same way (2^11-scaled low planes for P and V),
+ * FP32 accumulation and online softmax, output f32. */
+LDB_API int ldb_flash_attention_f32_workspace_size(int batch, int lq, int lk, int heads, int head_dim,
+                                                   size_t* bytes);
+LDB_API int ldb_flash_attention_f32(ldb_stream_t stream, const float* q, int q_ld, const float* k, const float* v,
+                                    int kv_ld, float* out, int out_ld, int batch, int lq, int lk, int heads,
+                                    int head_dim, float scale, void* workspace, size_t workspace_bytes);
+
 LDB_API int ldb_flash_attention_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes);
 LDB_API int ldb_flash_attention_ws(ldb_stream_t stream, const void* q, int q_ld, const void* k, const void* v,
                                    int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads,

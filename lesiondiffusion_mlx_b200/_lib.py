@@ -74,6 +74,8 @@ SIGNATURES: dict[str, list] = {
     "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
     "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],
     "ldb_flash_attention_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],
+    "ldb_flash_attention_f32_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],
+    "ldb_flash_attention_f32": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _P, _SZ],
     "ldb_flash_attention_ws": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ],
     "ldb_step_advance": [_P, _P],
     "ldb_timestep_embedding": [_P, _P, _P, _I, _I, _P, _I],

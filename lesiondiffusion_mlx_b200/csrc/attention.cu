@@ -7,8 +7,8 @@
 // blocks of 128 keys once for both.  Warp 0 issues the TMA loads (Q once,
 // K/V in a 3-stage ring); warp 1 issues the MMAs: S_t = Q_t K^T into a TMEM
 // score buffer per tile and O_t += P_t V (P from shared memory, V as an
-// MN-major operand).  Warps 2-5 run the online softmax of tile 0 and warps
-// 6-9 that of tile 1, one query row per thread: while one warpgroup turns
+// MN-major operand).  Warps 4-7 run the online softmax of tile 0 and warps
+// 8-11 that of tile 1, one query row per thread: while one warpgroup turns
 // its scores into probabilities, the tensor core works on the other tile.
 //
 // Softmax contract of _attention_half.py:58-113: FP32 scores, running max
@@ -29,26 +29,45 @@
 namespace ldb {
 namespace {
 
-constexpr int kAttnThreads = 320;  // producer, MMA, 2 x 4 softmax warps
+// Three warpgroups: WG0 = producer warp, MMA warp and two idle warps; WG1 and
+// WG2 = the softmax of query tiles 0 and 1.  Ten or twelve warps put three
+// warps on some SM sub-partitions, which caps a thread at 168 registers at
+// launch; WG0 gives registers up (setmaxnreg) so the softmax warps, which
+// hold a 128-score row each, get 224.  128 x 56 + 256 x 224 = 384 x 168.
+constexpr int kAttnThreads = 384;
+constexpr int kAttnLaunchRegs = 168;
+constexpr int kAttnRegsWg0 = 56;
+constexpr int kAttnRegsSoftmax = 224;
+static_assert(128 * kAttnRegsWg0 + 256 * kAttnRegsSoftmax <= kAttnThreads * kAttnLaunchRegs, "register split");
 constexpr int kBlockM = 128;       // queries per tile (two tiles per CTA)
 constexpr int kBlockN = 128;       // keys per block
 constexpr float kRescaleLog2 = 8.0f;
 
-template <int D>
+// SPLIT: FP32 attention in the split-f16 form (the reference's FP32 kernel,
+// _attention.py:148-280): every operand is two f16 planes, hi = f16(x) and a
+// low plane, loaded as separate tiles.  Scores take Qh Kh + Qh Kl + Ql Kh
+// into one FP32 accumulator (Q / K low planes unscaled, x - hi, so the three
+// products add directly); O keeps Ph Vh and the 2^11-scaled cross terms
+// Ph Vl' + Pl' Vh in two accumulators, combined as hi + lo / 2048 at the end.
+template <int D, bool SPLIT = false>
 struct AttnCfg {
+  static constexpr int kPlanes = SPLIT ? 2 : 1;
   static constexpr int kRowBytes = D * 2;
   static constexpr uint32_t kLayout = D == 64 ? kSwizzle128 : (D == 32 ? kSwizzle64 : kSwizzle32);
   static constexpr uint32_t kSbo = 8 * kRowBytes;  // K-major and MN-major 8-row group stride
-  static constexpr int kQBytes = kBlockM * kRowBytes;
-  static constexpr int kKBytes = kBlockN * kRowBytes;
-  static constexpr int kPBytes = kBlockM * kBlockN * 2;  // two 64-key SW128 chunks
-  static constexpr int kStages = 3;
-  // smem: Q0 Q1 | (K V) x stages | P0 P1 | barriers
-  static constexpr int kOffK = 2 * kQBytes;
-  static constexpr int kOffP = kOffK + kStages * 2 * kKBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  static constexpr int kQBytes = kBlockM * kRowBytes;    // one plane of a query tile
+  static constexpr int kKBytes = kBlockN * kRowBytes;    // one plane of a K or V block
+  static constexpr int kPBytes = kBlockM * kBlockN * 2;  // one plane of P: two 64-key SW128 chunks
+  static constexpr int kStages = SPLIT ? 2 : 3;
+  // smem: Q [tile][plane] | stages x (K planes, V planes) | P [tile][plane] | barriers
+  static constexpr int kOffK = 2 * kPlanes * kQBytes;
+  static constexpr int kStageBytes = 2 * kPlanes * kKBytes;
+  static constexpr int kOffP = kOffK + kStages * kStageBytes;
+  static constexpr int kOffBar = kOffP + 2 * kPlanes * kPBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-  static constexpr int kTmemCols = 512;  // S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [384, 384+D)
+  // S0 [0,128), S1 [128,256), O0 [256, 256 + planes*D), O1 [384, 384 + planes*D)
+  static constexpr int kTmemCols = 512;
+  static_assert(kSmemBytes <= 232448, "attention shared memory");
 };
 
 struct AttnParams {
@@ -65,11 +84,12 @@ struct AttnParams {
   float* ml_part;
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const AttnParams p, unsigned int* status) {
-  using Cfg = AttnCfg<D>;
+  using Cfg = AttnCfg<D, SPLIT>;
+  constexpr int kPl = Cfg::kPlanes;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,23 +143,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_begin();
 
+  // The register split sits at the top of each warpgroup's branch (one
+  // instruction for all four warps), so every role's code is compiled with
+  // its own budget.
+  if (warp < 4) {
+  regs_dec<kAttnRegsWg0>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t armed_mask = 0, armed_parity = 0;
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
-      tma_load_3d(smem, &qmap, q_full, h * D, q0, b);
-      tma_load_3d(smem + Cfg::kQBytes, &qmap, q_full, h * D, q0 + kBlockM, b);
+      mbar_arrive_expect_tx(q_full, 2 * kPl * Cfg::kQBytes);
+      // head h, plane pl starts at column (h * planes + pl) * D of the projection row
+      for (int t = 0; t < 2; ++t)
+        for (int pl = 0; pl < kPl; ++pl)
+          tma_load_3d(smem + (t * kPl + pl) * Cfg::kQBytes, &qmap, q_full, (h * kPl + pl) * D, q0 + t * kBlockM, b);
       for (int j = 0; j < nblocks; ++j) {
         const int st = j % Cfg::kStages;
         const uint32_t ph = (j / Cfg::kStages) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status)) break;
-        uint8_t* sk = smem + Cfg::kOffK + st * 2 * Cfg::kKBytes;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * Cfg::kKBytes);
+        uint8_t* sk = smem + Cfg::kOffK + st * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(&kv_full[st], Cfg::kStageBytes);
         armed_mask |= 1u << st;
         armed_parity = (armed_parity & ~(1u << st)) | (ph << st);
-        tma_load_3d(sk, &kmap, &kv_full[st], h * D, (jb0 + j) * kBlockN, b);
-        tma_load_3d(sk + Cfg::kKBytes, &vmap, &kv_full[st], h * D, (jb0 + j) * kBlockN, b);
+        for (int pl = 0; pl < kPl; ++pl) {
+          tma_load_3d(sk + pl * Cfg::kKBytes, &kmap, &kv_full[st], (h * kPl + pl) * D, (jb0 + j) * kBlockN, b);
+          tma_load_3d(sk + (kPl + pl) * Cfg::kKBytes, &vmap, &kv_full[st], (h * kPl + pl) * D,
+                      (jb0 + j) * kBlockN, b);
+        }
       }
       if (*abort_flag) {
         volatile int never = 0;
@@ -166,28 +196,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t p_addr = smem_u32(smem + Cfg::kOffP + t * Cfg::kPBytes);
-            const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + pst * 2 * Cfg::kKBytes + Cfg::kKBytes);
+            const uint32_t p_addr = smem_u32(smem + Cfg::kOffP + t * kPl * Cfg::kPBytes);
+            const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + pst * Cfg::kStageBytes + kPl * Cfg::kKBytes);
+            const uint32_t o_hi = tmem + 256 + t * 128;
+            // (P plane, V plane, accumulator): Ph Vh -> O_hi; split adds Ph Vl', Pl' Vh -> O_lo
+            constexpr int kTerms = SPLIT ? 3 : 1;
 #pragma unroll
-            for (int k = 0; k < kBlockN / 16; ++k) {
-              const uint64_t ad = make_smem_desc(p_addr + (k >> 2) * (kBlockM * 128) + (k & 3) * 32, 16, 1024,
-                                                 kSwizzle128);
-              const uint64_t bd = make_smem_desc(v_addr + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8,
-                                                 Cfg::kSbo, Cfg::kLayout);
-              umma_ss(tmem + 256 + t * 128, ad, bd, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
+            for (int term = 0; term < kTerms; ++term) {
+              const uint32_t pa = p_addr + (term == 2 ? Cfg::kPBytes : 0);
+              const uint32_t va = v_addr + (term == 1 ? Cfg::kKBytes : 0);
+              const uint32_t acc = o_hi + (term > 0 ? D : 0);
+#pragma unroll
+              for (int k = 0; k < kBlockN / 16; ++k) {
+                const uint64_t ad = make_smem_desc(pa + (k >> 2) * (kBlockM * 128) + (k & 3) * 32, 16, 1024,
+                                                   kSwizzle128);
+                const uint64_t bd = make_smem_desc(va + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8,
+                                                   Cfg::kSbo, Cfg::kLayout);
+                umma_ss(acc, ad, bd, idesc_pv, (j > 1 || k > 0 || term == 2) ? 1u : 0u);
+              }
             }
             umma_commit(&pv_done[t]);
             if (t == 1) umma_commit(&kv_empty[pst]);
           }
           if (j < nblocks) {
-            // S_t(j) = Q_t K_j^T
-            const uint32_t q_addr = smem_u32(smem + t * Cfg::kQBytes);
-            const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * 2 * Cfg::kKBytes);
+            // S_t(j) = Q_t K_j^T (split: Qh Kh + Qh Kl + Ql Kh)
+            const uint32_t q_addr = smem_u32(smem + t * kPl * Cfg::kQBytes);
+            const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * Cfg::kStageBytes);
+            constexpr int kTerms = SPLIT ? 3 : 1;
 #pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint64_t ad = make_smem_desc(q_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-              const uint64_t bd = make_smem_desc(k_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-              umma_ss(tmem + t * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+            for (int term = 0; term < kTerms; ++term) {
+              const uint32_t qa = q_addr + (term == 2 ? Cfg::kQBytes : 0);
+              const uint32_t ka = k_addr + (term == 1 ? Cfg::kKBytes : 0);
+#pragma unroll
+              for (int k = 0; k < D / 16; ++k) {
+                const uint64_t ad = make_smem_desc(qa + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+                const uint64_t bd = make_smem_desc(ka + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+                umma_ss(tmem + t * 128, ad, bd, idesc_qk, (k > 0 || term > 0) ? 1u : 0u);
+              }
             }
             umma_commit(&s_full[t]);
           }
@@ -197,15 +242,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       volatile int never = 0;
       mbar_wait(drain, 0, &never, status);
     }
+  }
   } else {
+  regs_inc<kAttnRegsSoftmax>();
+  {
     // ------------------------------------------------------------ softmax
-    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int t = (warp - 4) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;   // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tmem_s = tmem + t * 128 + lane_base;
     const uint32_t tmem_o = tmem + 256 + t * 128 + lane_base;
-    uint8_t* sp = smem + Cfg::kOffP + t * Cfg::kPBytes;
+    uint8_t* sp = smem + Cfg::kOffP + t * kPl * Cfg::kPBytes;
     const float c = p.scale_log2;
     float m_ref = -INFINITY;  // reference maximum (raw scores) of the probabilities in O and l
     float l = 0.f;
@@ -256,7 +304,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (__any_sync(0xffffffffu, grow)) {
           const float scale = grow ? alpha : 1.f;
 #pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 16) {
+          for (int c0 = 0; c0 < kPl * D; c0 += 16) {
             uint32_t r[16];
             tmem_ld16(tmem_o + c0, r);
             tmem_wait_ld();
@@ -276,6 +324,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c0 = 0; c0 < kBlockN; c0 += 32) {
         uint32_t packed[16];
+        uint32_t packed_lo[SPLIT ? 16 : 1];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c0 + i]), c, -mc));
@@ -287,6 +336,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           } else {
             __half2 v2 = __floats2half2_rn(e0, e1);
             packed[i / 2] = *reinterpret_cast<uint32_t*>(&v2);
+            if constexpr (SPLIT) {
+              const float2 hf = __half22float2(v2);
+              __half2 l2 = __floats2half2_rn((e0 - hf.x) * 2048.0f, (e1 - hf.y) * 2048.0f);
+              packed_lo[i / 2] = *reinterpret_cast<uint32_t*>(&l2);
+            }
           }
         }
         // Keys c0..c0+31 of this row: chunk c0/64, 16-byte units at the
@@ -298,6 +352,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int unit = (u0 + u) ^ (row & 7);
           *reinterpret_cast<uint4*>(chunk + unit * 16) =
               make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+          if constexpr (SPLIT)
+            *reinterpret_cast<uint4*>(chunk + Cfg::kPBytes + unit * 16) =
+                make_uint4(packed_lo[4 * u], packed_lo[4 * u + 1], packed_lo[4 * u + 2], packed_lo[4 * u + 3]);
         }
       }
       l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
@@ -307,7 +364,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(&p_ready[t]);
     }
     const bool done = ok && warp_wait(&pv_done[t], (nblocks - 1) & 1, abort_flag, status);
-    if (done && p.kv_splits > 1) {
+    if (done && p.kv_splits > 1 && !SPLIT) {
       // Partial over this CTA's keys: raw O row, reference max and sum.
       tc_fence_after();
       const int qrow = q0 + t * kBlockM + row;
@@ -326,6 +383,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       if (qrow < p.lq) *reinterpret_cast<float2*>(p.ml_part + prow * 2) = make_float2(m_ref, l);
+    } else if (done && SPLIT) {
+      tc_fence_after();
+      const int qrow = q0 + t * kBlockM + row;
+      const float inv = 1.f / l;
+      float* out = static_cast<float*>(p.out) + (static_cast<long long>(b) * p.lq + qrow) * p.out_ld + h * D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 16) {
+        uint32_t r[16], lo[16];
+        tmem_ld16(tmem_o + c0, r);
+        tmem_ld16(tmem_o + D + c0, lo);
+        tmem_wait_ld();
+        if (qrow < p.lq) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            float4 o;
+            o.x = (__uint_as_float(r[i]) + __uint_as_float(lo[i]) * (1.0f / 2048.0f)) * inv;
+            o.y = (__uint_as_float(r[i + 1]) + __uint_as_float(lo[i + 1]) * (1.0f / 2048.0f)) * inv;
+            o.z = (__uint_as_float(r[i + 2]) + __uint_as_float(lo[i + 2]) * (1.0f / 2048.0f)) * inv;
+            o.w = (__uint_as_float(r[i + 3]) + __uint_as_float(lo[i + 3]) * (1.0f / 2048.0f)) * inv;
+            *reinterpret_cast<float4*>(out + c0 + i) = o;
+          }
+        }
+      }
     } else if (done) {
       tc_fence_after();
       const int qrow = q0 + t * kBlockM + row;
@@ -356,6 +436,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     tc_fence_before();
+  }
   }
 
   __syncwarp();
@@ -398,6 +479,37 @@ __global__ void attn_combine_kernel(const AttnParams p) {
   if (lane + 32 < D) out[lane + 32] = static_cast<T>(a1 * inv);
 }
 
+// FP32 projections -> split f16 planes for the SPLIT kernel.  src is
+// (rows, H*D) f32 with row stride src_ld; dst is (rows, H*2D) f16 with head
+// h at columns [2hD, 2hD + D) (hi) and [2hD + D, 2hD + 2D) (low): hi =
+// f16(x * mul), low = f16((x * mul - hi) * lo_scale).  One thread per 8
+// elements.
+__global__ void attn_split_kernel(const float* src, int src_ld, long long rows, int heads, int d, float mul,
+                                  float lo_scale, __half* dst) {
+  pdl_begin();
+  const int vecs = heads * d / 8;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows * vecs) return;
+  const long long r = idx / vecs;
+  const int col = static_cast<int>(idx - r * vecs) * 8;
+  const int hh = col / d, c = col - hh * d;
+  const float4 a = *reinterpret_cast<const float4*>(src + r * src_ld + col);
+  const float4 b = *reinterpret_cast<const float4*>(src + r * src_ld + col + 4);
+  const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint4 hi_raw, lo_raw;
+  __half* hi = reinterpret_cast<__half*>(&hi_raw);
+  __half* lo = reinterpret_cast<__half*>(&lo_raw);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float v = x[j] * mul;
+    hi[j] = __float2half_rn(v);
+    lo[j] = __float2half_rn((v - __half2float(hi[j])) * lo_scale);
+  }
+  __half* o = dst + r * (2LL * heads * d) + 2LL * hh * d + c;
+  *reinterpret_cast<uint4*>(o) = hi_raw;
+  *reinterpret_cast<uint4*>(o + d) = lo_raw;
+}
+
 // Key splits for a grid of `ctas` CTAs over `blocks` key blocks.  Splitting
 // costs a partial write, a merge launch and per-CTA set-up, which only pays
 // when the unsplit grid leaves most SMs idle (measured: 32 CTAs of 800
@@ -413,15 +525,27 @@ int choose_kv_splits(long long ctas, int blocks) {
   return (blocks + bps - 1) / bps;  // ranges that get key blocks
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool SPLIT = false>
 int launch_attn(cudaStream_t stream, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                 const AttnParams& p) {
-  using Cfg = AttnCfg<D>;
-  auto kernel = flash_attn_kernel<D, BF16>;
+  using Cfg = AttnCfg<D, SPLIT>;
+  auto kernel = flash_attn_kernel<D, BF16, SPLIT>;
   static unsigned long long configured = 0;
-  const int rc = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), Cfg::kSmemBytes, &configured,
-                                       "attention smem attribute");
+  int rc = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), Cfg::kSmemBytes, &configured,
+                                 "attention smem attribute");
   if (rc != LDB_OK) return rc;
+  // The warpgroups' register split must fit the registers the CTA is
+  // launched with, or the softmax warps' setmaxnreg.inc would wait forever.
+  static int launch_regs = 0;
+  if (launch_regs == 0) {
+    cudaFuncAttributes attr;
+    rc = check_cuda(cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(kernel)), "attention attributes");
+    if (rc != LDB_OK) return rc;
+    launch_regs = attr.numRegs;
+  }
+  if (launch_regs * kAttnThreads < 128 * kAttnRegsWg0 + 256 * kAttnRegsSoftmax)
+    return fail(LDB_ERR_CUDA, "attention kernel launches with %d registers per thread; the register split needs %d",
+                launch_regs, kAttnLaunchRegs);
   dim3 grid(((p.lq + 2 * kBlockM - 1) / (2 * kBlockM)) * p.kv_splits, p.heads, p.batch);
   int r = launch_kernel(kernel, grid, dim3(kAttnThreads), Cfg::kSmemBytes, stream, "attention launch", qm, km, vm,
                         p, device_status_ptr());
@@ -521,6 +645,85 @@ int ldb_flash_attention_ws(cudaStream_t stream, const void* q, int q_ld, const v
                            int dtype, void* workspace, size_t workspace_bytes) {
   return flash_attention_impl(stream, q, q_ld, k, v, kv_ld, out, out_ld, batch, lq, lk, heads, head_dim, scale, dtype,
                               workspace, workspace_bytes);
+}
+
+int ldb_flash_attention_f32_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes) {
+  using namespace ldb;
+  if (!bytes) return fail(LDB_ERR_INVALID, "bytes is null");
+  if (batch <= 0 || lq <= 0 || lk <= 0 || heads <= 0 || head_dim <= 0)
+    return fail(LDB_ERR_SHAPE, "extents must be positive");
+  // split planes of Q, K and V: (rows, heads * 2 * head_dim) f16 each
+  *bytes = static_cast<size_t>(batch) * (static_cast<size_t>(lq) + 2 * lk) * heads * head_dim * 2 * 2;
+  return LDB_OK;
+}
+
+int ldb_flash_attention_f32(cudaStream_t stream, const float* q, int q_ld, const float* k, const float* v,
+                            int kv_ld, float* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim,
+                            float scale, void* workspace, size_t workspace_bytes) {
+  using namespace ldb;
+  if (!q || !k || !v || !out || !workspace) return fail(LDB_ERR_INVALID, "flash_attention_f32: null pointer");
+  if (head_dim != 32) return fail(LDB_ERR_SHAPE, "FP32 attention takes 32-wide heads (got %d)", head_dim);
+  if (batch <= 0 || lq <= 0 || lk <= 0 || heads <= 0) return fail(LDB_ERR_SHAPE, "extents must be positive");
+  if (q_ld < heads * head_dim || kv_ld < heads * head_dim || out_ld < heads * head_dim)
+    return fail(LDB_ERR_SHAPE, "row strides must cover heads * head_dim");
+  if (q_ld % 4 || kv_ld % 4 || out_ld % 4) return fail(LDB_ERR_ALIGNMENT, "row strides must be multiples of 4");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(out)) % 16)
+    return fail(LDB_ERR_ALIGNMENT, "FP32 attention pointers must be 16-byte aligned");
+  size_t need = 0;
+  int rc = ldb_flash_attention_f32_workspace_size(batch, lq, lk, heads, head_dim, &need);
+  if (rc != LDB_OK) return rc;
+  if (workspace_bytes < need) return fail(LDB_ERR_WORKSPACE, "FP32 attention needs %zu workspace bytes", need);
+  const int width = heads * head_dim * 2;  // split row width in f16
+  __half* qs = static_cast<__half*>(workspace);
+  __half* ks = qs + static_cast<size_t>(batch) * lq * width;
+  __half* vs = ks + static_cast<size_t>(batch) * lk * width;
+  const int threads = 256;
+  const float log2e = 1.4426950408889634f;
+  struct Part {
+    const float* src;
+    int ld;
+    long long rows;
+    float mul, lo_scale;
+    __half* dst;
+  } parts[3] = {{q, q_ld, static_cast<long long>(batch) * lq, scale * log2e, 1.0f, qs},
+                {k, kv_ld, static_cast<long long>(batch) * lk, 1.0f, 1.0f, ks},
+                {v, kv_ld, static_cast<long long>(batch) * lk, 1.0f, 2048.0f, vs}};
+  for (const Part& pt : parts) {
+    const long long n = pt.rows * heads * head_dim / 8;
+    rc = launch_kernel(attn_split_kernel, dim3(static_cast<unsigned>((n + threads - 1) / threads)), dim3(threads), 0,
+                       stream, "attention split launch", pt.src, pt.ld, pt.rows, heads, head_dim, pt.mul, pt.lo_scale,
+                       pt.dst);
+    if (rc != LDB_OK) return rc;
+  }
+  const uint32_t box[3] = {static_cast<uint32_t>(head_dim), 128u, 1u};
+  CUtensorMap qm, km, vm;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(width), static_cast<uint64_t>(lq), static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(width) * 2, static_cast<uint64_t>(lq) * width * 2};
+    rc = encode_tiled_f16(&qm, qs, 3, dims, strides, box, head_dim * 2, false);
+    if (rc != LDB_OK) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(width), static_cast<uint64_t>(lk), static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(width) * 2, static_cast<uint64_t>(lk) * width * 2};
+    rc = encode_tiled_f16(&km, ks, 3, dims, strides, box, head_dim * 2, false);
+    if (rc != LDB_OK) return rc;
+    rc = encode_tiled_f16(&vm, vs, 3, dims, strides, box, head_dim * 2, false);
+    if (rc != LDB_OK) return rc;
+  }
+  AttnParams p;
+  p.batch = batch;
+  p.heads = heads;
+  p.lq = lq;
+  p.lk = lk;
+  p.out_ld = out_ld;
+  p.scale_log2 = 1.0f;  // Q carries scale * log2(e)
+  p.out = out;
+  p.kv_splits = 1;
+  p.blocks_per_split = (lk + kBlockN - 1) / kBlockN;
+  p.o_part = p.ml_part = nullptr;
+  return launch_attn<32, false, true>(stream, qm, km, vm, p);
 }
 
 }  // extern "C"

@@ -96,6 +96,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Register reallocation between warpgroups (all four warps of a warpgroup
+// execute the same instruction).  The counts must be multiples of 8 in
+// [24, 256], and the warpgroups' totals after the change must not exceed the
+// registers the CTA was launched with (threads x registers per thread).
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Warp-collective wait: every lane waits, then the warp reconverges and
 // agrees on the outcome, so the `.sync.aligned` tcgen05 instructions that
 // follow always run with the full warp.

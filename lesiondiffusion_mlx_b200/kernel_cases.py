@@ -44,6 +44,7 @@ ATTN_CASES = {
     "cross_6400x77_bf16": (1, 6400, 77, 8, 64, torch.bfloat16),
     "self_6400_h4": (1, 6400, 6400, 4, 64, torch.float16),
     "self_800_h8": (1, 800, 800, 8, 64, torch.float16),
+    "lmnet_self_23104_f32": (1, 23104, 23104, 2, 32, torch.float32),  # LMNet's FP32 level (16 x 38 x 38)
 }
 
 

@@ -180,11 +180,17 @@ def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: fl
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, scale: float,
                     out: torch.Tensor | None = None) -> torch.Tensor:
-    """``softmax(q k^T * scale) v`` per head on projection-layout ``(B, L, H*D)`` tensors."""
+    """``softmax(q k^T * scale) v`` per head on projection-layout ``(B, L, H*D)`` tensors.
+
+    float16 / bfloat16 inputs run the tcgen05 flash kernel directly; float32
+    inputs (32-wide heads, the reference's FP32 kernel, _attention.py:148-375)
+    run it in the split-f16 form and return float32."""
     if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
         raise ValueError("attention inputs are (B, L, heads * head_dim)")
+    if q.dtype == torch.float32 and k.dtype == q.dtype and v.dtype == q.dtype:
+        return _flash_attention_f32(q, k, v, heads=heads, scale=scale, out=out)
     if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
-        raise ValueError("attention inputs must share dtype float16 or bfloat16")
+        raise ValueError("attention inputs must share dtype float16, bfloat16 or float32")
     batch, lq, width = (int(s) for s in q.shape)
     lk = int(k.shape[1])
     if width % heads:
@@ -204,6 +210,31 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
             "ldb_flash_attention_ws", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
             int(k.stride(1)), out.data_ptr(), int(out.stride(1)), batch, lq, lk, heads, width // heads,
             float(scale), _DT[q.dtype], _ptr(ws), ws_bytes.value,
+        )
+    return out
+
+
+def _flash_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, scale: float,
+                         out: torch.Tensor | None) -> torch.Tensor:
+    batch, lq, width = (int(s) for s in q.shape)
+    lk = int(k.shape[1])
+    if width != heads * 32:
+        raise ValueError("FP32 attention takes 32-wide heads")
+    if k.stride(1) != v.stride(1) or k.stride(0) != v.stride(0):
+        raise ValueError("k and v must share strides")
+    for t in (q, k, v):
+        if t.stride(2) != 1 or t.stride(0) != t.shape[1] * t.stride(1):
+            raise ValueError("attention inputs must be row-major with unit column stride")
+    if out is None:
+        out = torch.empty((batch, lq, width), dtype=torch.float32, device=q.device)
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.call("ldb_flash_attention_f32_workspace_size", batch, lq, lk, heads, 32, ctypes.byref(ws_bytes))
+    ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=q.device)
+    with instrument.maybe_time("attention", 4.0 * batch * lq * lk * width):
+        _lib.call(
+            "ldb_flash_attention_f32", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
+            int(k.stride(1)), out.data_ptr(), int(out.stride(1)), batch, lq, lk, heads, 32, float(scale),
+            ws.data_ptr(), ws_bytes.value,
         )
     return out
 

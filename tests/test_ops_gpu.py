@@ -99,6 +99,42 @@ def test_layer_norm(cuda_device):
 
 
 @pytest.mark.parametrize(
+    "batch,lq,lk,heads,qscale",
+    [
+        (1, 96, 96, 2, 2.0),
+        (2, 300, 200, 2, 2.0),  # partial query and key tiles
+        (1, 640, 77, 2, 2.0),  # cross-attention, one partial key block
+        (1, 2048, 2048, 4, 6.0),  # peaked softmax: the running maximum moves
+        (1, 23104, 23104, 2, 1.0),  # LMNet's 16 x 38 x 38 level, 2 heads of 32
+    ],
+)
+def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale):
+    """FP32 attention (split-f16 tensor-core products) against float64 softmax
+    attention at the FP32 tolerance (rel-L2 <= 1e-4; measured ~1e-6)."""
+    from lesiondiffusion_mlx_b200 import ops
+
+    d = 32
+    rng = np.random.default_rng(lq + 3 * lk)
+    q = (rng.normal(size=(batch, lq, heads * d)) * qscale).astype(np.float32)
+    k = rng.normal(size=(batch, lk, heads * d)).astype(np.float32)
+    v = rng.normal(size=(batch, lk, heads * d)).astype(np.float32)
+    scale = d ** -0.5
+    got = ops.flash_attention(*(torch.from_numpy(a).to(cuda_device) for a in (q, k, v)), heads=heads, scale=scale)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    got = got.cpu().numpy()
+    rows = np.arange(lq)
+    if lq > 1024:
+        rows = np.unique(np.concatenate([np.arange(200), np.arange(lq - 150, lq), np.arange(0, lq, 211)]))
+    exact = oracle_ops.attention(torch.from_numpy(q[:, rows]).double(), torch.from_numpy(k).double(),
+                                 torch.from_numpy(v).double(), heads=heads, scale=scale).numpy()
+    assert np.all(np.isfinite(got))
+    err = rel_l2(got[:, rows], exact)
+    assert err <= 1e-4, err
+    np.testing.assert_allclose(got[:, rows], exact, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize(
     "batch,lq,lk,heads,d,dtype,ties",
     [
         (1, 96, 96, 2, 32, torch.float16, False),
