@@ -7,7 +7,7 @@
 // blocks of 128 keys once for both.  Warp 0 issues the TMA loads (Q once,
 // K/V in a 3-stage ring); warp 1 issues the MMAs: S_t = Q_t K^T into a TMEM
 // score buffer per tile and O_t += P_t V (P from shared memory, V as an
-// MN-major operand).  Warps 4-7 run the online softmax of tile 0 and warps
+// MN-major operand, P from TMEM).  Warps 4-7 run the online softmax of tile 0 and warps
 // 8-11 that of tile 1, one query row per thread: while one warpgroup turns
 // its scores into probabilities, the tensor core works on the other tile.
 //
@@ -57,15 +57,16 @@ struct AttnCfg {
   static constexpr uint32_t kSbo = 8 * kRowBytes;  // K-major and MN-major 8-row group stride
   static constexpr int kQBytes = kBlockM * kRowBytes;    // one plane of a query tile
   static constexpr int kKBytes = kBlockN * kRowBytes;    // one plane of a K or V block
-  static constexpr int kPBytes = kBlockM * kBlockN * 2;  // one plane of P: two 64-key SW128 chunks
-  static constexpr int kStages = SPLIT ? 2 : 3;
-  // smem: Q [tile][plane] | stages x (K planes, V planes) | P [tile][plane] | barriers
+  static constexpr int kStages = SPLIT ? 3 : 4;
+  // smem: Q [tile][plane] | stages x (K planes, V planes) | barriers
   static constexpr int kOffK = 2 * kPlanes * kQBytes;
   static constexpr int kStageBytes = 2 * kPlanes * kKBytes;
-  static constexpr int kOffP = kOffK + kStages * kStageBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPlanes * kPBytes;
-  static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-  // S0 [0,128), S1 [128,256), O0 [256, 256 + planes*D), O1 [384, 384 + planes*D)
+  static constexpr int kOffBar = kOffK + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers: 2 kStages + 8 words, then the TMEM slot
+  static_assert((2 * kStages + 8) * 8 + 16 <= 256, "attention barrier block");
+  // TMEM: S0 [0,128), S1 [128,256), O0 [256, 256 + planes*D), O1 [384, 384 + planes*D).
+  // The probabilities overwrite their scores as packed 16-bit pairs: P_t
+  // plane 0 in columns [128t, 128t + 64), plane 1 in [128t + 64, 128t + 128).
   static constexpr int kTmemCols = 512;
   static_assert(kSmemBytes <= 232448, "attention shared memory");
 };
@@ -94,14 +95,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  constexpr int kS = Cfg::kStages;
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [3]
-  uint64_t* kv_empty = bars + 4;   // [3]
-  uint64_t* s_full = bars + 7;     // [2] per query tile
-  uint64_t* p_ready = bars + 9;    // [2]
-  uint64_t* pv_done = bars + 11;   // [2]
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* kv_full = bars + 1;             // [kStages]
+  uint64_t* kv_empty = kv_full + kS;        // [kStages]
+  uint64_t* s_full = kv_empty + kS;         // [2] per query tile
+  uint64_t* p_ready = s_full + 2;           // [2]
+  uint64_t* pv_done = p_ready + 2;          // [2]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -196,23 +198,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t p_addr = smem_u32(smem + Cfg::kOffP + t * kPl * Cfg::kPBytes);
+            const uint32_t p_tmem = tmem + t * 128;  // P_t overwrote S_t
             const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + pst * Cfg::kStageBytes + kPl * Cfg::kKBytes);
             const uint32_t o_hi = tmem + 256 + t * 128;
             // (P plane, V plane, accumulator): Ph Vh -> O_hi; split adds Ph Vl', Pl' Vh -> O_lo
             constexpr int kTerms = SPLIT ? 3 : 1;
 #pragma unroll
             for (int term = 0; term < kTerms; ++term) {
-              const uint32_t pa = p_addr + (term == 2 ? Cfg::kPBytes : 0);
+              const uint32_t pa = p_tmem + (term == 2 ? 64 : 0);
               const uint32_t va = v_addr + (term == 1 ? Cfg::kKBytes : 0);
               const uint32_t acc = o_hi + (term > 0 ? D : 0);
 #pragma unroll
               for (int k = 0; k < kBlockN / 16; ++k) {
-                const uint64_t ad = make_smem_desc(pa + (k >> 2) * (kBlockM * 128) + (k & 3) * 32, 16, 1024,
-                                                   kSwizzle128);
+                // 16 keys = 8 TMEM columns of packed pairs
                 const uint64_t bd = make_smem_desc(va + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8,
                                                    Cfg::kSbo, Cfg::kLayout);
-                umma_ss(acc, ad, bd, idesc_pv, (j > 1 || k > 0 || term == 2) ? 1u : 0u);
+                umma_ts(acc, pa + k * 8, bd, idesc_pv, (j > 1 || k > 0 || term == 2) ? 1u : 0u);
               }
             }
             umma_commit(&pv_done[t]);
@@ -253,7 +254,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tmem_s = tmem + t * 128 + lane_base;
     const uint32_t tmem_o = tmem + 256 + t * 128 + lane_base;
-    uint8_t* sp = smem + Cfg::kOffP + t * kPl * Cfg::kPBytes;
     const float c = p.scale_log2;
     float m_ref = -INFINITY;  // reference maximum (raw scores) of the probabilities in O and l
     float l = 0.f;
@@ -343,22 +343,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
         }
-        // Keys c0..c0+31 of this row: chunk c0/64, 16-byte units at the
-        // 128-byte-swizzled positions of row `row`.
-        uint8_t* chunk = sp + (c0 >> 6) * (kBlockM * 128) + (row >> 3) * 1024 + (row & 7) * 128;
-        const int u0 = (c0 & 63) >> 3;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int unit = (u0 + u) ^ (row & 7);
-          *reinterpret_cast<uint4*>(chunk + unit * 16) =
-              make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-          if constexpr (SPLIT)
-            *reinterpret_cast<uint4*>(chunk + Cfg::kPBytes + unit * 16) =
-                make_uint4(packed_lo[4 * u], packed_lo[4 * u + 1], packed_lo[4 * u + 2], packed_lo[4 * u + 3]);
-        }
+        // Keys c0..c0+31 of this row: 16 packed pairs over its scores (all
+        // of which are already in registers).
+        tmem_st16(tmem_s + (c0 >> 1), packed);
+        if constexpr (SPLIT) tmem_st16(tmem_s + 64 + (c0 >> 1), packed_lo);
       }
       l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[t]);
