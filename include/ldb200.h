@@ -205,6 +205,13 @@ LDB_API int ldb_prepare_input_from_stats(ldb_stream_t stream, const void* x1, in
 LDB_API int ldb_layer_norm(ldb_stream_t stream, const void* x, int x_ld, const float* gamma, const float* beta,
                            float eps, void* out, int out_ld, int rows, int channels);
 
+/* LayerNorm of f16 or f32 rows (x_dtype LDB_F16 / LDB_F32) in FP32; with
+ * split = 1 the f16 output row holds the hi plane then the 2^11-scaled low
+ * plane, each padded to a multiple of 16 channels (the FP32-exact conv input,
+ * as ldb_prepare_input writes it), for the FP32 network. */
+LDB_API int ldb_layer_norm_ex(ldb_stream_t stream, const void* x, int x_dtype, int x_ld, const float* gamma,
+                              const float* beta, float eps, void* out, int out_ld, int rows, int channels, int split);
+
 /* -------------------------------------------------------------------------
  * Attention: replaces flash_attention / flash_attention_half
  * (_attention.py:331-375, _attention_half.py:129-147) and the fused SDPA
@@ -223,7 +230,7 @@ LDB_API int ldb_flash_attention(ldb_stream_t stream, const void* q, int q_ld, co
  * _attention_half.py:58-113 across key ranges).  With a null or too small
  * workspace it runs unsplit.  Workspace bytes from
  * ldb_flash_attention_workspace_size (0: no split would help). */
-/* FP32 attention for 32-wide heads (the reference's FP32 flash_attention,
+/* FP32 attention for 16-, 32- or 64-wide heads (the reference's FP32 flash_attention,
  * _attention.py:148-375): q, k, v, out are f32 projections (B, L, H*32) with
  * row strides q_ld / kv_ld / out_ld (multiples of 4, 16-byte aligned
  * pointers).  Runs the tcgen05 kernel in split-f16 form: Q * scale * log2(e),
@@ -279,6 +286,15 @@ LDB_API int ldb_sampler_step(ldb_stream_t stream, int kind, float* x, float* pre
                              const float* noise, long long noise_step_stride, const float* mask,
                              const float* image, int image_channels, void* net_in, int in_ld, int batch,
                              int voxels, int channels, const float* coeff_table, const int* step);
+
+/* ldb_sampler_step for either network: eps_dtype LDB_F16 or LDB_F32 (the
+ * FP32 LMNet prediction); with net_split = 1 the next network input is
+ * written as the FP32-exact conv input, the f16 hi plane then the 2^11-scaled
+ * low plane of the input channels padded to a multiple of 16. */
+LDB_API int ldb_sampler_step_ex(ldb_stream_t stream, int kind, float* x, float* prev, const void* eps, int eps_dtype,
+                                int eps_ld, const float* noise, long long noise_step_stride, const float* mask,
+                                const float* image, int image_channels, void* net_in, int in_ld, int net_split,
+                                int batch, int voxels, int channels, const float* coeff_table, const int* step);
 
 /* Nearest 4-channel codebook search with the straight-through quantize
  * (nearest_codebook4, _vq.py:64-82; VqAutoencoder.quantize,

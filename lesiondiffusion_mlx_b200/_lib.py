@@ -71,6 +71,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_prepare_input": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I],
     "ldb_group_norm_affine_from_stats": [_P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _F, _P],
     "ldb_prepare_input_from_stats": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _F, _I, _I, _P, _I],
+    "ldb_layer_norm_ex": [_P, _P, _I, _I, _P, _P, _F, _P, _I, _I, _I, _I],
     "ldb_layer_norm": [_P, _P, _I, _P, _P, _F, _P, _I, _I, _I],
     "ldb_flash_attention": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I],
     "ldb_flash_attention_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],
@@ -80,6 +81,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_step_advance": [_P, _P],
     "ldb_timestep_embedding": [_P, _P, _P, _I, _I, _P, _I],
     "ldb_dense_small": [_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I],
+    "ldb_sampler_step_ex": [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_longlong, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _P],
     "ldb_sampler_step": [_P, _I, _P, _P, _P, _I, _P, ctypes.c_longlong, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P],
     "ldb_vq_nearest4": [_P, _P, _I, ctypes.c_longlong, _P, _I, _I, _P, _P, _I],
     "ldb_resize_nearest": [_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _I, _I],

@@ -57,7 +57,7 @@ struct AttnCfg {
   static constexpr uint32_t kSbo = 8 * kRowBytes;  // K-major and MN-major 8-row group stride
   static constexpr int kQBytes = kBlockM * kRowBytes;    // one plane of a query tile
   static constexpr int kKBytes = kBlockN * kRowBytes;    // one plane of a K or V block
-  static constexpr int kStages = SPLIT ? 3 : 4;
+  static constexpr int kStages = SPLIT ? (D == 64 ? 2 : 3) : 4;
   // smem: Q [tile][plane] | stages x (K planes, V planes) | barriers
   static constexpr int kOffK = 2 * kPlanes * kQBytes;
   static constexpr int kStageBytes = 2 * kPlanes * kKBytes;
@@ -653,7 +653,8 @@ int ldb_flash_attention_f32(cudaStream_t stream, const float* q, int q_ld, const
                             float scale, void* workspace, size_t workspace_bytes) {
   using namespace ldb;
   if (!q || !k || !v || !out || !workspace) return fail(LDB_ERR_INVALID, "flash_attention_f32: null pointer");
-  if (head_dim != 32) return fail(LDB_ERR_SHAPE, "FP32 attention takes 32-wide heads (got %d)", head_dim);
+  if (head_dim != 16 && head_dim != 32 && head_dim != 64)
+    return fail(LDB_ERR_SHAPE, "FP32 attention takes heads 16, 32 or 64 wide (got %d)", head_dim);
   if (batch <= 0 || lq <= 0 || lk <= 0 || heads <= 0) return fail(LDB_ERR_SHAPE, "extents must be positive");
   if (q_ld < heads * head_dim || kv_ld < heads * head_dim || out_ld < heads * head_dim)
     return fail(LDB_ERR_SHAPE, "row strides must cover heads * head_dim");
@@ -714,6 +715,8 @@ int ldb_flash_attention_f32(cudaStream_t stream, const float* q, int q_ld, const
   p.kv_splits = 1;
   p.blocks_per_split = (lk + kBlockN - 1) / kBlockN;
   p.o_part = p.ml_part = nullptr;
+  if (head_dim == 64) return launch_attn<64, false, true>(stream, qm, km, vm, p);
+  if (head_dim == 16) return launch_attn<16, false, true>(stream, qm, km, vm, p);
   return launch_attn<32, false, true>(stream, qm, km, vm, p);
 }
 

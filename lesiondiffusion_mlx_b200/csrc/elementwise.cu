@@ -121,25 +121,41 @@ __global__ void dense_small_kernel(const __half* x, int x_ld, const __half* w, c
 // With a mask, composition re-imposes the known region (x*m + (1-m)*image,
 // mlx_sampling.py:119, :134-135); the next network input
 // [x | extra] is written as f16 with channel stride in_ld (zero padded),
-// where `extra` is the mask (inpainting) or the conditioning image.
+// where `extra` is the mask (inpainting) or the conditioning image; for the
+// FP32 network (net_cpad > 0) it is written as the f16 hi plane in channels
+// [0, net_cpad) and the 2^11-scaled low plane in [net_cpad, 2 net_cpad).
+// eps is the network's f16 or f32 prediction.
 struct StepArgs {
   const float* coeff;  // [steps][5] f32 coefficient table (device)
   const int* step;     // current step index (device), or null for step 0
   long long noise_step_stride;  // elements between the noise of consecutive steps
   float* x;            // (B, V, C) f32 state, updated in place
   float* prev;         // (B, V, C) f32 DPM history
-  const __half* eps;   // (B, V, eps_ld) f16 prediction (first C channels used)
+  const void* eps;     // (B, V, eps_ld) f16 or f32 prediction (first C channels used)
   int eps_ld;
+  int eps_f32;
   const float* noise;  // (B, V, C) f32
   const float* mask;   // (B, V) f32 or null
   const float* image;  // (B, V, C) f32 known-region latent, or the concatenated image (B, V, extra_c)
   int image_c;         // channels of `image`
   __half* net_in;      // (B, V, in_ld) f16 or null
   int in_ld;
+  int net_cpad;        // > 0: split FP32 input planes of net_cpad channels each
   long long voxels;    // B * V
   int channels;
   int kind;
 };
+
+__device__ __forceinline__ void put_net_in(const StepArgs& a, long long v, int c, float x) {
+  const __half hi = __float2half_rn(x);
+  a.net_in[v * a.in_ld + c] = hi;
+  if (a.net_cpad > 0) a.net_in[v * a.in_ld + a.net_cpad + c] = __float2half_rn((x - __half2float(hi)) * 2048.0f);
+}
+
+__device__ __forceinline__ float load_eps(const StepArgs& a, long long v, int c) {
+  return a.eps_f32 ? static_cast<const float*>(a.eps)[v * a.eps_ld + c]
+                   : __half2float(static_cast<const __half*>(a.eps)[v * a.eps_ld + c]);
+}
 
 __global__ void sampler_step_kernel(StepArgs a) {
   pdl_begin();
@@ -162,13 +178,13 @@ __global__ void sampler_step_kernel(StepArgs a) {
     const long long i = v * C + c;
     float x = a.x[i];
     if (a.kind == 1) {
-      const float e = __half2float(a.eps[v * a.eps_ld + c]);
+      const float e = load_eps(a, v, c);
       // k0 = alpha, k1 = previous, k2 = sigma, k3 = sqrt(1 - alpha)
       const float pred = __fdiv_rn(__fsub_rn(x, __fmul_rn(k3, e)), sqrtf(k0));
       const float dir = __fmul_rn(sqrtf(__fsub_rn(__fsub_rn(1.f, k1), __fmul_rn(k2, k2))), e);
       x = __fadd_rn(__fadd_rn(__fmul_rn(sqrtf(k1), pred), dir), __fmul_rn(k2, noise[i]));
     } else if (a.kind == 2) {
-      const float e = __half2float(a.eps[v * a.eps_ld + c]);
+      const float e = load_eps(a, v, c);
       // (alpha, sigma, ratio, clean, history)
       const float pred = __fdiv_rn(__fsub_rn(x, __fmul_rn(k1, e)), k0);
       x = __fadd_rn(__fadd_rn(__fmul_rn(k2, x), __fmul_rn(k3, pred)), __fmul_rn(k4, __fsub_rn(pred, a.prev[i])));
@@ -176,16 +192,16 @@ __global__ void sampler_step_kernel(StepArgs a) {
     }
     if (a.mask) x = __fadd_rn(__fmul_rn(x, m), __fmul_rn(__fsub_rn(1.f, m), a.image[i]));
     a.x[i] = x;
-    if (a.net_in) a.net_in[v * a.in_ld + c] = __float2half_rn(x);
+    if (a.net_in) put_net_in(a, v, c, x);
   }
   if (a.net_in) {
     int c = C;
     if (a.mask) {
-      a.net_in[v * a.in_ld + c++] = __float2half_rn(m);
+      put_net_in(a, v, c++, m);
     } else {
-      for (int j = 0; j < a.image_c; ++j) a.net_in[v * a.in_ld + c++] = __float2half_rn(a.image[v * a.image_c + j]);
+      for (int j = 0; j < a.image_c; ++j) put_net_in(a, v, c++, a.image[v * a.image_c + j]);
     }
-    for (; c < a.in_ld; ++c) a.net_in[v * a.in_ld + c] = __float2half_rn(0.f);
+    for (; c < (a.net_cpad > 0 ? a.net_cpad : a.in_ld); ++c) put_net_in(a, v, c, 0.f);
   }
 }
 
@@ -373,43 +389,54 @@ int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w,
                        n_out, k, in_silu, out_silu, int(out_dtype == LDB_F32), round_f16);
 }
 
-int ldb_sampler_step(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_ld,
-                     const float* noise, long long noise_step_stride, const float* mask, const float* image,
-                     int image_channels, void* net_in, int in_ld, int batch, int voxels, int channels,
-                     const float* coeff_table, const int* step) {
+int ldb_sampler_step_ex(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_dtype,
+                        int eps_ld, const float* noise, long long noise_step_stride, const float* mask,
+                        const float* image, int image_channels, void* net_in, int in_ld, int net_split, int batch,
+                        int voxels, int channels, const float* coeff_table, const int* step) {
   using namespace ldb;
   if (kind < 0 || kind > 2) return fail(LDB_ERR_INVALID, "sampler step kind %d", kind);
   if (!x || channels <= 0 || batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "sampler_step: bad extents");
   if (kind >= 1 && (!eps || !coeff_table || eps_ld < channels))
     return fail(LDB_ERR_INVALID, "sampler_step: eps/coeff");
+  if (eps_dtype != LDB_F16 && eps_dtype != LDB_F32) return fail(LDB_ERR_INVALID, "sampler_step: eps dtype");
   if (kind == 1 && !noise) return fail(LDB_ERR_INVALID, "DDIM step needs noise");
   if (kind == 2 && !prev) return fail(LDB_ERR_INVALID, "DPM step needs the history buffer");
   if ((mask || net_in) && !image && (mask || image_channels > 0))
     return fail(LDB_ERR_INVALID, "sampler_step: image is required");
-  if (net_in) {
-    const int need = channels + (mask ? 1 : image_channels);
-    if (in_ld < need) return fail(LDB_ERR_SHAPE, "in_ld %d < %d network input channels", in_ld, need);
-  }
+  const int need = channels + (mask ? 1 : image_channels);
+  const int cpad = net_split ? (need + 15) / 16 * 16 : 0;
+  if (net_in && in_ld < (net_split ? 2 * cpad : need))
+    return fail(LDB_ERR_SHAPE, "in_ld %d too small for %d network input channels", in_ld, need);
   StepArgs a{};
   a.coeff = coeff_table;
   a.step = step;
   a.noise_step_stride = noise_step_stride;
   a.x = x;
   a.prev = prev;
-  a.eps = static_cast<const __half*>(eps);
+  a.eps = eps;
   a.eps_ld = eps_ld;
+  a.eps_f32 = eps_dtype == LDB_F32;
   a.noise = noise;
   a.mask = mask;
   a.image = image;
   a.image_c = mask ? channels : image_channels;
   a.net_in = static_cast<__half*>(net_in);
   a.in_ld = in_ld;
+  a.net_cpad = cpad;
   a.voxels = static_cast<long long>(batch) * voxels;
   a.channels = channels;
   a.kind = kind;
   const int threads = 256;
   return launch_kernel(sampler_step_kernel, dim3(static_cast<unsigned>((a.voxels + threads - 1) / threads)),
                        dim3(threads), 0, stream, "sampler_step launch", a);
+}
+
+int ldb_sampler_step(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_ld,
+                     const float* noise, long long noise_step_stride, const float* mask, const float* image,
+                     int image_channels, void* net_in, int in_ld, int batch, int voxels, int channels,
+                     const float* coeff_table, const int* step) {
+  return ldb_sampler_step_ex(stream, kind, x, prev, eps, LDB_F16, eps_ld, noise, noise_step_stride, mask, image,
+                             image_channels, net_in, in_ld, 0, batch, voxels, channels, coeff_table, step);
 }
 
 int ldb_vq_nearest4(cudaStream_t stream, const void* z, int z_ld, long long positions, const void* codebook,

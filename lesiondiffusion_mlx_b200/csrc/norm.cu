@@ -383,30 +383,41 @@ __global__ void prepare_stats_kernel(Src2 s, int voxels, int stat_voxels, const 
 
 // LayerNorm over the last axis of (rows, C) f16 (mlx_model.py:360-367):
 // FP32 statistics, one rounding.  One warp per row; C <= 1024, C % 8 == 0.
-__global__ void layer_norm_kernel(const __half* x, int x_ld, const float* gamma, const float* beta, float eps,
-                                  __half* out, int out_ld, int rows, int C) {
+template <bool F32_IN, bool SPLIT_OUT>
+__global__ void layer_norm_kernel(const void* x_, int x_ld, const float* gamma, const float* beta, float eps,
+                                  __half* out, int out_ld, int rows, int C, int cpad) {
   pdl_begin();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
-  const __half* xr = x + static_cast<long long>(warp) * x_ld;
   float v[32];
-  int n = 0;
   float sum = 0.f;
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int c = (it * 32 + lane) * 8;
     if (c < C) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
-      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+      if constexpr (F32_IN) {
+        const float* xr = static_cast<const float*>(x_) + static_cast<long long>(warp) * x_ld;
+        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __half22float2(h[q]);
-        v[it * 8 + 2 * q] = f.x;
-        v[it * 8 + 2 * q + 1] = f.y;
-        sum += f.x + f.y;
+        for (int j = 0; j < 8; ++j) {
+          v[it * 8 + j] = f[j];
+          sum += f[j];
+        }
+      } else {
+        const __half* xr = static_cast<const __half*>(x_) + static_cast<long long>(warp) * x_ld;
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(h[q]);
+          v[it * 8 + 2 * q] = f.x;
+          v[it * 8 + 2 * q + 1] = f.y;
+          sum += f.x + f.y;
+        }
       }
-      n += 8;
     }
   }
 #pragma unroll
@@ -431,20 +442,21 @@ __global__ void layer_norm_kernel(const __half* x, int x_ld, const float* gamma,
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int c = (it * 32 + lane) * 8;
-    if (c < C) {
-      uint4 raw;
-      __half2* h = reinterpret_cast<__half2*>(&raw);
+    if (c < (SPLIT_OUT ? cpad : C)) {
+      uint4 raw, lo_raw;
+      __half* h = reinterpret_cast<__half*>(&raw);
+      __half* lo = reinterpret_cast<__half*>(&lo_raw);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = it * 8 + 2 * q;
-        const float a = (v[j] - mean) * rstd * gamma[c + 2 * q] + beta[c + 2 * q];
-        const float b2 = (v[j + 1] - mean) * rstd * gamma[c + 2 * q + 1] + beta[c + 2 * q + 1];
-        h[q] = __floats2half2_rn(a, b2);
+      for (int j = 0; j < 8; ++j) {
+        float y = 0.f;
+        if (c < C) y = (v[it * 8 + j] - mean) * rstd * gamma[c + j] + beta[c + j];
+        h[j] = __float2half_rn(y);
+        if constexpr (SPLIT_OUT) lo[j] = __float2half_rn((y - __half2float(h[j])) * 2048.0f);
       }
       *reinterpret_cast<uint4*>(orow + c) = raw;
+      if constexpr (SPLIT_OUT) *reinterpret_cast<uint4*>(orow + cpad + c) = lo_raw;
     }
   }
-  (void)n;
 }
 
 int make_src(const void* x1, int c1, int ld1, const void* x2, int c2, int ld2, int dtype, Src2* s) {
@@ -631,18 +643,27 @@ int ldb_prepare_input_from_stats(cudaStream_t stream, const void* x1, int c1, in
                        gamma, beta, eps, silu, split, cpad, static_cast<__half*>(out), out_ld);
 }
 
-int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,
-                   void* out, int out_ld, int rows, int channels) {
+int ldb_layer_norm_ex(cudaStream_t stream, const void* x, int x_dtype, int x_ld, const float* gamma,
+                      const float* beta, float eps, void* out, int out_ld, int rows, int channels, int split) {
   using namespace ldb;
   if (!x || !out || !gamma || !beta) return fail(LDB_ERR_INVALID, "layer_norm: null pointer");
+  if (x_dtype != LDB_F16 && x_dtype != LDB_F32) return fail(LDB_ERR_INVALID, "layer_norm input must be f16 or f32");
   if (channels <= 0 || channels > 1024 || channels % 8) return fail(LDB_ERR_SHAPE, "channels must be 8..1024, %% 8");
+  const int cpad = split ? (channels + 15) / 16 * 16 : channels;
   if (x_ld % 8 || out_ld % 8) return fail(LDB_ERR_ALIGNMENT, "row strides must be multiples of 8");
+  if (out_ld < (split ? 2 * cpad : channels)) return fail(LDB_ERR_SHAPE, "out_ld too small");
   if (rows <= 0) return fail(LDB_ERR_SHAPE, "rows must be positive");
   const int threads = 256;
   const long long blocks = (static_cast<long long>(rows) * 32 + threads - 1) / threads;
-  return launch_kernel(layer_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, stream,
-                       "layer_norm launch", static_cast<const __half*>(x), x_ld, gamma, beta, eps,
-                       static_cast<__half*>(out), out_ld, rows, channels);
+  auto kernel = x_dtype == LDB_F32 ? (split ? layer_norm_kernel<true, true> : layer_norm_kernel<true, false>)
+                                   : (split ? layer_norm_kernel<false, true> : layer_norm_kernel<false, false>);
+  return launch_kernel(kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, stream, "layer_norm launch", x,
+                       x_ld, gamma, beta, eps, static_cast<__half*>(out), out_ld, rows, channels, cpad);
+}
+
+int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* gamma, const float* beta, float eps,
+                   void* out, int out_ld, int rows, int channels) {
+  return ldb_layer_norm_ex(stream, x, LDB_F16, x_ld, gamma, beta, eps, out, out_ld, rows, channels, 0);
 }
 
 // GroupNorm affine without any allocation: the same statistics as

@@ -110,11 +110,25 @@ def _voxels(x: torch.Tensor) -> tuple[int, int, int]:
 
 
 _GN_STATS = "_ldb_gn_stats"  # attribute of a conv output that carries its GroupNorm statistics
+# Attribute of a tensor in the FP32-exact conv input format (f16 hi plane then
+# 2^11-scaled low plane, each padded to 16 channels): its channel count.
+_SPLIT_C = "_ldb_split_c"
+
+
+def _mark_split(t: torch.Tensor, channels: int) -> torch.Tensor:
+    setattr(t, _SPLIT_C, channels)
+    return t
 
 
 class _Layers:
+    """Layer helpers shared by the networks.  With float32 weights (``exact``)
+    every conv and dense layer runs the FP32-exact split-f16 conv, activations
+    are f32, and the inputs of those layers are written in the split format
+    (by the norm pass, the LayerNorm, or an explicit split pass)."""
+
     def __init__(self, params: _Params):
         self.p = params
+        self.exact = params.dtype == torch.float32
         # Per-forward float64 arena (zeroed once per forward) that conv outputs
         # feeding a GroupNorm take their statistics slices from.
         self._arena: torch.Tensor | None = None
@@ -143,11 +157,24 @@ class _Layers:
         ``pad01`` pads a stride-2 conv with zeros only after each axis."""
         packed = self.p.conv(key, stride)
         st = self._take_stats(int(x.shape[0]), packed.out_channels) if stats else None
+        x, cin = self._conv_input(x)
         out = conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
-                           output_scale=output_scale, stats=st, pad01=pad01)
+                           output_scale=output_scale, stats=st, pad01=pad01, in_channels=cin)
         if st is not None:
             setattr(out, _GN_STATS, st)
         return out
+
+    def _conv_input(self, x: torch.Tensor) -> tuple[torch.Tensor, int | None]:
+        """(conv input, its channel count for the split format) of an activation."""
+        if not self.exact:
+            return x, None
+        c = getattr(x, _SPLIT_C, None)
+        if c is None:
+            c = int(x.shape[-1])
+            if c % 8:  # the split pass reads 8-channel groups: zero-pad the rows
+                x = torch.nn.functional.pad(x, (0, 8 - c % 8))
+            x = ops.prepare_input(x, split=True)
+        return x, c
 
     def group_norm_input(self, x: torch.Tensor, norm_key: str, *, groups: int, eps: float, silu: bool,
                          x2: torch.Tensor | None = None) -> torch.Tensor:
@@ -157,11 +184,14 @@ class _Layers:
         gamma, beta = self.p.f32(norm_key + ".weight"), self.p.f32(norm_key + ".bias")
         st1 = getattr(x, _GN_STATS, None)
         st2 = None if x2 is None else getattr(x2, _GN_STATS, None)
+        channels = int(x.shape[-1]) + (0 if x2 is None else int(x2.shape[-1]))
         if st1 is not None and (x2 is None or st2 is not None):
-            return ops.prepare_input_from_stats(x, st1, gamma, beta, groups=groups, eps=eps, silu=silu, x2=x2,
-                                                stats2=st2)
-        affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=eps, x2=x2)
-        return ops.prepare_input(x, affine=affine, silu=silu, x2=x2)
+            out = ops.prepare_input_from_stats(x, st1, gamma, beta, groups=groups, eps=eps, silu=silu, x2=x2,
+                                               stats2=st2, split=self.exact)
+        else:
+            affine = ops.group_norm_affine(x, gamma, beta, groups=groups, eps=eps, x2=x2)
+            out = ops.prepare_input(x, affine=affine, silu=silu, x2=x2, split=self.exact)
+        return _mark_split(out, channels) if self.exact else out
 
     def norm_silu_conv(self, x: torch.Tensor, norm_key: str, conv_key: str, *, groups: int, eps: float,
                        shift: torch.Tensor | None = None, residual: torch.Tensor | None = None,
@@ -176,20 +206,26 @@ class _Layers:
         """Linear layer(s) on token rows (B, L, C) via the pointwise tensor-core conv."""
         packed = self.p.dense_packed(*keys)
         bias = self.p.dense_bias(*keys)
-        b, length, c = (int(s) for s in x.shape)
+        x, cin = self._conv_input(x)
+        b, length = int(x.shape[0]), int(x.shape[1])
         x5 = x.unsqueeze(1).unsqueeze(1)
         res5 = None if residual is None else residual.unsqueeze(1).unsqueeze(1)
-        out = conv3d_ndhwc(x5, packed, bias, residual=res5, act=act)
+        out = conv3d_ndhwc(x5, packed, bias, residual=res5, act=act, in_channels=cin)
         return out.view(b, length, packed.out_channels)
 
 
 class LdmUnetB200(_Layers):
-    """The LDM UNet (mlx_model.py:384-654) on B200 kernels, NDHWC f16."""
+    """The LDM UNet (mlx_model.py:384-654) on B200 kernels, NDHWC.
+
+    float16 is the LINet arithmetic; float32 is LMNet's FP32 stage
+    (medmlx.py:1168-1257): FP32-exact split-f16 convs and dense layers, FP32
+    split-f16 attention, f32 activations.  The float32 network takes its
+    input in the split format (``split_input``), as the sampler writes it."""
 
     def __init__(self, weights: dict[str, torch.Tensor], config: UnetConfig, *, device: torch.device | str = "cuda",
                  dtype: torch.dtype = torch.float16):
-        if dtype != torch.float16:
-            raise ValueError("the B200 UNet runs in float16 (the LINet checkpoint dtype)")
+        if dtype not in (torch.float16, torch.float32):
+            raise ValueError("the B200 UNet runs in float16 (LINet) or float32 (LMNet)")
         super().__init__(_Params(weights, torch.device(device), dtype))
         self.config = config
         self.device = torch.device(device)
@@ -202,6 +238,7 @@ class LdmUnetB200(_Layers):
         """Stack every residual block's ``emb_layers.1`` so one skinny GEMM per step
         produces all per-block shifts (they all read the same ``silu(emb)``)."""
         keys = sorted(n[: -len(".emb_layers.1.weight")] for n in self.p.raw if n.endswith(".emb_layers.1.weight"))
+        self._emb_keys = tuple(k + ".emb_layers.1" for k in keys)
         offsets: dict[str, tuple[int, int]] = {}
         weights, biases, start = [], [], 0
         for key in keys:
@@ -234,14 +271,35 @@ class LdmUnetB200(_Layers):
 
     # ------------------------------------------------------------- blocks
 
+    def split_input(self, x: torch.Tensor) -> torch.Tensor:
+        """The network input in the format ``forward`` takes: f16 as is; for the
+        float32 network the split planes of f32 ``x``."""
+        if not self.exact:
+            return x
+        split, c = self._conv_input(x)
+        return _mark_split(split, c)
+
+    def _rows_dense(self, x: torch.Tensor, *keys: str, silu: bool = False) -> torch.Tensor:
+        """FP32 dense layer on (B, C) rows (``silu`` applied to the input first)."""
+        c = int(x.shape[-1])
+        xs = ops.prepare_input(x, silu=silu, split=True).view(int(x.shape[0]), 1, 1, 1, -1)
+        out = conv3d_ndhwc(xs, self.p.dense_packed(*keys), self.p.dense_bias(*keys), in_channels=c)
+        return out.view(int(x.shape[0]), -1)
+
     def time_embedding(self, timesteps: torch.Tensor, step: torch.Tensor | None = None) -> torch.Tensor:
         """mlx_model.py:609-614; ``timesteps`` int32 (B,) or a (steps, B) table read at ``*step``."""
+        if self.exact:
+            emb = ops.timestep_embedding(timesteps, self.config.model_channels, step=step, out_dtype=torch.float32)
+            h = self._rows_dense(emb, "time_embed.0")
+            return self._rows_dense(h, "time_embed.2", silu=True)
         emb = ops.timestep_embedding(timesteps, self.config.model_channels, step=step, out_dtype=torch.float16)
         h = ops.dense_small(emb, self.p.f16("time_embed.0.weight"), self.p.f32("time_embed.0.bias"))
         return ops.dense_small(h, self.p.f16("time_embed.2.weight"), self.p.f32("time_embed.2.bias"), in_silu=True)
 
     def block_shifts(self, emb: torch.Tensor) -> torch.Tensor:
         """All residual blocks' ``dense(silu(emb), emb_layers.1)`` in one launch, f16-rounded f32."""
+        if self.exact:
+            return self._rows_dense(emb, *self._emb_keys, silu=True)
         return ops.dense_small(emb, self._emb_weight, self._emb_bias, in_silu=True, out_dtype=torch.float32,
                                round_f16=True)
 
@@ -258,7 +316,11 @@ class LdmUnetB200(_Layers):
         out_c = int(h.shape[-1])
         groups = 32 if out_c % 32 == 0 else out_c
         if self.p.has(key + ".skip_connection.weight"):
-            cat = x if x2 is None else ops.prepare_input(x, x2=x2)
+            cat = x
+            if x2 is not None:
+                cat = ops.prepare_input(x, x2=x2, split=self.exact)
+                if self.exact:
+                    _mark_split(cat, int(x.shape[-1]) + int(x2.shape[-1]))
             skip = self.conv(cat, key + ".skip_connection")
         else:
             skip = x
@@ -268,7 +330,7 @@ class LdmUnetB200(_Layers):
     def attention(self, x: torch.Tensor, key: str, heads: int, kv: tuple[torch.Tensor, torch.Tensor] | None,
                   residual: torch.Tensor) -> torch.Tensor:
         """``residual + to_out(attention(x, context))`` (mlx_model.py:443-493)."""
-        c = int(x.shape[-1])
+        c = getattr(x, _SPLIT_C, None) or int(x.shape[-1])
         if kv is None:
             qkv = self.dense(x, key + ".to_q", key + ".to_k", key + ".to_v")
             q, k, v = qkv[..., :c], qkv[..., c : 2 * c], qkv[..., 2 * c :]
@@ -290,7 +352,9 @@ class LdmUnetB200(_Layers):
         blk = key + ".transformer_blocks.0"
 
         def ln(t_: torch.Tensor, n: str) -> torch.Tensor:
-            return ops.layer_norm(t_, self.p.f32(f"{blk}.{n}.weight"), self.p.f32(f"{blk}.{n}.bias"), 1e-5)
+            out = ops.layer_norm(t_, self.p.f32(f"{blk}.{n}.weight"), self.p.f32(f"{blk}.{n}.bias"), 1e-5,
+                                 split=self.exact)
+            return _mark_split(out, c) if self.exact else out
 
         tokens = self.attention(ln(tokens, "norm1"), blk + ".attn1", heads, None, tokens)
         tokens = self.attention(ln(tokens, "norm2"), blk + ".attn2", heads, cache.get(blk + ".attn2"), tokens)
@@ -302,9 +366,13 @@ class LdmUnetB200(_Layers):
         """Project the context and every attn2 K/V once per binding (mlx_model.py:570-597)."""
         if context is None or self.config.skip_context:
             return {}
-        ctx = context.to(self.device, torch.float16).contiguous()
-        if ctx.shape[-1] % 8:
-            ctx = torch.nn.functional.pad(ctx, (0, 8 - ctx.shape[-1] % 8))[..., : context.shape[-1]]
+        ctx = context.to(self.device, torch.float32 if self.exact else torch.float16).contiguous()
+        width = int(context.shape[-1])
+        if width % 8:
+            ctx = torch.nn.functional.pad(ctx, (0, 8 - width % 8))
+            # f16: a channel view of the zero-padded rows; FP32: split planes of
+            # the padded rows (the zero channels meet zero weight rows)
+            ctx = _mark_split(ops.prepare_input(ctx, split=True), width) if self.exact else ctx[..., :width]
         projected = self.dense(ctx, "context_linear_projection")
         cache = {}
         for name in self.p.raw:

@@ -163,18 +163,23 @@ def prepare_input_from_stats(
 
 
 def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
-               out: torch.Tensor | None = None) -> torch.Tensor:
-    """Last-axis LayerNorm of f16 rows; ``gamma``/``beta`` f32."""
-    if x.dtype != torch.float16:
-        raise ValueError("layer_norm expects float16")
+               out: torch.Tensor | None = None, split: bool = False) -> torch.Tensor:
+    """Last-axis LayerNorm of f16 or f32 rows in FP32; ``gamma``/``beta`` f32.
+
+    The output is f16; with ``split`` it holds the hi plane then the
+    2^11-scaled low plane (each padded to 16 channels), the input format of
+    the FP32-exact conv."""
+    if x.dtype not in (torch.float16, torch.float32):
+        raise ValueError("layer_norm expects float16 or float32")
     voxels, c, ld = _rows(x)
     rows = int(x.shape[0]) * voxels
+    cpad = (c + 15) // 16 * 16
     if out is None:
-        out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+        out = torch.empty((*x.shape[:-1], 2 * cpad if split else c), dtype=torch.float16, device=x.device)
     _, _, out_ld = _rows(out)
     with instrument.maybe_time("layer_norm", 0.0):
-        _lib.call("ldb_layer_norm", _stream(x), x.data_ptr(), ld, gamma.data_ptr(), beta.data_ptr(), float(eps),
-                  out.data_ptr(), out_ld, rows, c)
+        _lib.call("ldb_layer_norm_ex", _stream(x), x.data_ptr(), _DT[x.dtype], ld, gamma.data_ptr(), beta.data_ptr(),
+                  float(eps), out.data_ptr(), out_ld, rows, c, int(split))
     return out
 
 
@@ -183,7 +188,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
     """``softmax(q k^T * scale) v`` per head on projection-layout ``(B, L, H*D)`` tensors.
 
     float16 / bfloat16 inputs run the tcgen05 flash kernel directly; float32
-    inputs (32-wide heads, the reference's FP32 kernel, _attention.py:148-375)
+    inputs (16-, 32- or 64-wide heads; the reference's FP32 kernel, _attention.py:148-375)
     run it in the split-f16 form and return float32."""
     if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
         raise ValueError("attention inputs are (B, L, heads * head_dim)")
@@ -218,8 +223,9 @@ def _flash_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, h
                          out: torch.Tensor | None) -> torch.Tensor:
     batch, lq, width = (int(s) for s in q.shape)
     lk = int(k.shape[1])
-    if width != heads * 32:
-        raise ValueError("FP32 attention takes 32-wide heads")
+    if width % heads or width // heads not in (16, 32, 64):
+        raise ValueError("FP32 attention takes heads 16, 32 or 64 wide")
+    d = width // heads
     if k.stride(1) != v.stride(1) or k.stride(0) != v.stride(0):
         raise ValueError("k and v must share strides")
     for t in (q, k, v):
@@ -228,12 +234,12 @@ def _flash_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, h
     if out is None:
         out = torch.empty((batch, lq, width), dtype=torch.float32, device=q.device)
     ws_bytes = ctypes.c_size_t(0)
-    _lib.call("ldb_flash_attention_f32_workspace_size", batch, lq, lk, heads, 32, ctypes.byref(ws_bytes))
+    _lib.call("ldb_flash_attention_f32_workspace_size", batch, lq, lk, heads, d, ctypes.byref(ws_bytes))
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=q.device)
     with instrument.maybe_time("attention", 4.0 * batch * lq * lk * width):
         _lib.call(
             "ldb_flash_attention_f32", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
-            int(k.stride(1)), out.data_ptr(), int(out.stride(1)), batch, lq, lk, heads, 32, float(scale),
+            int(k.stride(1)), out.data_ptr(), int(out.stride(1)), batch, lq, lk, heads, d, float(scale),
             ws.data_ptr(), ws_bytes.value,
         )
     return out
@@ -275,9 +281,13 @@ def sampler_step(
     kind: int, x: torch.Tensor, *, eps: torch.Tensor | None = None, prev: torch.Tensor | None = None,
     noise: torch.Tensor | None = None, noise_step_stride: int = 0, mask: torch.Tensor | None = None,
     image: torch.Tensor | None = None, net_in: torch.Tensor | None = None, coeff: torch.Tensor | None = None,
-    step: torch.Tensor | None = None,
+    step: torch.Tensor | None = None, net_split: bool = False,
 ) -> None:
-    """One fused sampler step over the f32 state ``x`` (B, V..., C) (see ldb_sampler_step)."""
+    """One fused sampler step over the f32 state ``x`` (B, V..., C) (see ldb_sampler_step_ex).
+
+    ``eps`` is the f16 or f32 prediction; with ``net_split`` the next network
+    input is written in the FP32-exact split format (hi plane, then 2^11-scaled
+    low plane, each padded to 16 channels)."""
     voxels, channels, _ = _rows(x)
     batch = int(x.shape[0])
     eps_ld = 0
@@ -291,9 +301,10 @@ def sampler_step(
         _, _, in_ld = _rows(net_in)
     with instrument.maybe_time("sampler_step", 0.0):
         _lib.call(
-            "ldb_sampler_step", _stream(x), kind, x.data_ptr(), _ptr(prev), _ptr(eps), eps_ld, _ptr(noise),
-            int(noise_step_stride), _ptr(mask), _ptr(image), image_c, _ptr(net_in), in_ld, batch, voxels,
-            channels, _ptr(coeff), _ptr(step),
+            "ldb_sampler_step_ex", _stream(x), kind, x.data_ptr(), _ptr(prev), _ptr(eps),
+            _DT[eps.dtype] if eps is not None else _lib.LDB_F16, eps_ld, _ptr(noise), int(noise_step_stride),
+            _ptr(mask), _ptr(image), image_c, _ptr(net_in), in_ld, int(net_split), batch, voxels, channels,
+            _ptr(coeff), _ptr(step),
         )
 
 

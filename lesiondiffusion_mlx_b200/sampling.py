@@ -154,13 +154,19 @@ class PreparedSampler:
         dev = unet.device
         b, d, h, w, c = (int(s) for s in image.shape)
         extra = 1 if mask is not None else c
-        width = (c + extra + 7) // 8 * 8
         steps = sampler.steps
-        net_buf = torch.zeros((b, d, h, w, width), dtype=torch.float16, device=dev)
+        # The FP32 network (LMNet) takes its input as split hi / low planes.
+        self.net_split = bool(getattr(unet, "exact", False))
+        if self.net_split:
+            net_in = torch.zeros((b, d, h, w, 2 * ((c + extra + 15) // 16 * 16)), dtype=torch.float16, device=dev)
+            setattr(net_in, "_ldb_split_c", c + extra)
+        else:
+            width = (c + extra + 7) // 8 * 8
+            net_in = torch.zeros((b, d, h, w, width), dtype=torch.float16, device=dev)[..., : c + extra]
         self.state = SamplerState(
             x=torch.zeros((b, d, h, w, c), dtype=torch.float32, device=dev),
             prev=torch.zeros((b, d, h, w, c), dtype=torch.float32, device=dev),
-            net_in=net_buf[..., : c + extra],
+            net_in=net_in,
             noise=torch.zeros((steps, b, d, h, w, c), dtype=torch.float32, device=dev),
             coeff=torch.from_numpy(np.ascontiguousarray(sampler.coefficients)).to(dev),
             timesteps=torch.tensor([[t] * b for t in sampler.execution_timesteps], dtype=torch.int32, device=dev),
@@ -179,7 +185,7 @@ class PreparedSampler:
         ops.sampler_step(
             self.sampler.kind, s.x, eps=self.eps, prev=s.prev, noise=s.noise,
             noise_step_stride=int(s.noise[0].numel()), mask=s.mask, image=s.image, net_in=s.net_in,
-            coeff=s.coeff, step=s.step,
+            coeff=s.coeff, step=s.step, net_split=self.net_split,
         )
         ops.step_advance(s.step)
 
@@ -191,7 +197,7 @@ class PreparedSampler:
         if step_noise is not None and self.sampler.kind == KIND_DDIM:
             s.noise.copy_(step_noise.to(s.noise.device, torch.float32))
         s.step.zero_()
-        ops.sampler_step(KIND_COMPOSE, s.x, mask=s.mask, image=s.image, net_in=s.net_in)
+        ops.sampler_step(KIND_COMPOSE, s.x, mask=s.mask, image=s.image, net_in=s.net_in, net_split=self.net_split)
 
     def capture(self) -> None:
         """Capture one denoise step as a CUDA graph (after one eager warm-up step)."""

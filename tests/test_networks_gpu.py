@@ -176,6 +176,52 @@ def test_unet_baseline_shape_matches_oracle(cuda_device, skip_context):
     assert rel_l2(got, ref) <= 1e-2
 
 
+def test_fp32_unet_matches_reference_recording(cuda_device):
+    """The FP32 network (LMNet's arithmetic: split-f16 convs, dense layers and
+    attention) against the reference's FP32 Torch-CPU recording."""
+    from lesiondiffusion_mlx_b200.networks import LdmUnetB200, UnetConfig
+
+    f = golden("unet_mask")
+    assert f["dtype"].item() == "float32"
+    cfg = json.loads(f["config"].item())
+    config = UnetConfig(cfg["model_channels"], cfg["num_res_blocks"], tuple(cfg["attention_resolutions"]),
+                        tuple(cfg["channel_mult"]), cfg["num_head_channels"], cfg["skip_context"])
+    raw = unet_fixture_weights(int(f["weight_seed"]), skip_context=config.skip_context)
+    model = LdmUnetB200(torch_weights(raw, torch.float32), config, device=cuda_device, dtype=torch.float32)
+    x = torch.from_numpy(f["x"]).permute(0, 2, 3, 4, 1).contiguous().to(cuda_device)
+    t = torch.from_numpy(f["timesteps"].astype(np.int32)).to(cuda_device)
+    out = model(x, t, torch.from_numpy(f["context"]))
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32
+    got = out.permute(0, 4, 1, 2, 3).cpu().numpy()
+    want = f["output"].astype(np.float64)
+    assert rel_l2(got, want) <= 1e-4
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-5)
+
+
+def test_fp32_unet_lmnet_shape_matches_oracle(cuda_device):
+    """LMNet's topology (16 channels, one residual block per level, attention
+    at the 4x level and the middle, 32-wide heads, context) at a small crop,
+    FP32, against the oracle's FP32 network (rel-L2 <= 1e-4)."""
+    from lesiondiffusion_mlx_b200.networks import LdmUnetB200, UnetConfig
+
+    config = UnetConfig(16, 1, (4,), (1, 2, 4), 32, False)
+    raw = random_unet_weights(config, 4, 1, 768, seed=300)
+    model = LdmUnetB200(torch_weights(raw, torch.float32), config, device=cuda_device, dtype=torch.float32)
+    rng = np.random.default_rng(301)
+    x = rng.normal(size=(1, 4, 16, 24, 24)).astype(np.float32)
+    t = np.array([531], np.int32)
+    ctx = rng.normal(size=(1, 8, 768)).astype(np.float32)
+    xin = model.split_input(torch.from_numpy(x).permute(0, 2, 3, 4, 1).contiguous().to(cuda_device))
+    out = model(xin, torch.from_numpy(t).to(cuda_device), torch.from_numpy(ctx))
+    torch.cuda.synchronize()
+    got = out.permute(0, 4, 1, 2, 3).cpu().numpy()
+    oracle = OracleUnet(torch_weights(raw, torch.float32), OracleConfig(16, 1, (4,), (1, 2, 4), 32, False))
+    ref = oracle(torch.from_numpy(x), torch.from_numpy(t), torch.from_numpy(ctx)).double().numpy()
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) <= 1e-4
+
+
 @pytest.mark.parametrize("quantize", [True, False])
 def test_vq_decoder_matches_reference_recording(cuda_device, quantize):
     from lesiondiffusion_mlx_b200.networks import VqDecoderB200

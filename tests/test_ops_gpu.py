@@ -99,21 +99,22 @@ def test_layer_norm(cuda_device):
 
 
 @pytest.mark.parametrize(
-    "batch,lq,lk,heads,qscale",
+    "batch,lq,lk,heads,qscale,d",
     [
-        (1, 96, 96, 2, 2.0),
-        (2, 300, 200, 2, 2.0),  # partial query and key tiles
-        (1, 640, 77, 2, 2.0),  # cross-attention, one partial key block
-        (1, 2048, 2048, 4, 6.0),  # peaked softmax: the running maximum moves
-        (1, 23104, 23104, 2, 1.0),  # LMNet's 16 x 38 x 38 level, 2 heads of 32
+        (1, 96, 96, 2, 2.0, 16),
+        (1, 96, 96, 2, 2.0, 32),
+        (2, 520, 300, 2, 2.0, 64),
+        (2, 300, 200, 2, 2.0, 32),  # partial query and key tiles
+        (1, 640, 77, 2, 2.0, 32),  # cross-attention, one partial key block
+        (1, 2048, 2048, 4, 6.0, 32),  # peaked softmax: the running maximum moves
+        (1, 23104, 23104, 2, 1.0, 32),  # LMNet's 16 x 38 x 38 level, 2 heads of 32
     ],
 )
-def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale):
+def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale, d):
     """FP32 attention (split-f16 tensor-core products) against float64 softmax
     attention at the FP32 tolerance (rel-L2 <= 1e-4; measured ~1e-6)."""
     from lesiondiffusion_mlx_b200 import ops
 
-    d = 32
     rng = np.random.default_rng(lq + 3 * lk)
     q = (rng.normal(size=(batch, lq, heads * d)) * qscale).astype(np.float32)
     k = rng.normal(size=(batch, lk, heads * d)).astype(np.float32)
