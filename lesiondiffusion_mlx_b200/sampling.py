@@ -152,8 +152,12 @@ class PreparedSampler:
         self.cache = cache
         self.graph_enabled = graph
         dev = unet.device
-        b, d, h, w, c = (int(s) for s in image.shape)
-        extra = 1 if mask is not None else c
+        b, d, h, w, ci = (int(s) for s in image.shape)
+        # Inpainting (mask given): the state has the image's channels and the
+        # network reads [x | mask]; generation (no mask, LMNet): a one-channel
+        # state and [x | conditioning image] (mlx_sampling.py:105-110).
+        c = ci if mask is not None else 1
+        extra = 1 if mask is not None else ci
         steps = sampler.steps
         # The FP32 network (LMNet) takes its input as split hi / low planes.
         self.net_split = bool(getattr(unet, "exact", False))

@@ -222,6 +222,45 @@ def test_fp32_unet_lmnet_shape_matches_oracle(cuda_device):
     assert rel_l2(got, ref) <= 1e-4
 
 
+def test_fp32_lmnet_sampler_matches_oracle_trajectory(cuda_device):
+    """Four DDIM steps of the FP32 LMNet-shaped network through the prepared
+    sampler (CUDA-graph replay, split network input) against the oracle's
+    trajectory with the oracle's FP32 network and the same injected noise."""
+    from lesiondiffusion_mlx_b200.networks import LdmUnetB200, UnetConfig
+    from lesiondiffusion_mlx_b200.sampling import DdimSampler, PreparedSampler
+    from oracle import samplers as oracle_samplers
+
+    config = UnetConfig(16, 1, (4,), (1, 2, 4), 32, False)
+    raw = random_unet_weights(config, 4, 1, 768, seed=310)
+    model = LdmUnetB200(torch_weights(raw, torch.float32), config, device=cuda_device, dtype=torch.float32)
+    rng = np.random.default_rng(311)
+    cond = rng.random(size=(1, 3, 8, 16, 16)).astype(np.float32)
+    ctx = rng.normal(size=(1, 8, 768)).astype(np.float32)
+    init = rng.normal(size=(1, 1, 8, 16, 16)).astype(np.float32)
+    betas = np.linspace(0.00085 ** 0.5, 0.012 ** 0.5, 1000, dtype=np.float64) ** 2
+    alphas = np.cumprod(1.0 - betas).astype(np.float32)
+    steps = 4
+    noise = rng.normal(size=(steps, 1, 1, 8, 16, 16)).astype(np.float32)
+    sampler = DdimSampler(alphas, steps)
+    cache = model.prepare_context(torch.from_numpy(ctx).to(cuda_device))
+    prepared = PreparedSampler(sampler, model, cache, torch.from_numpy(cond).permute(0, 2, 3, 4, 1).to(cuda_device),
+                               None, graph=True)
+    to_ndhwc = lambda a: torch.from_numpy(a).permute(0, 2, 3, 4, 1)  # noqa: E731
+    out = prepared.run(to_ndhwc(init).to(cuda_device),
+                       torch.stack([to_ndhwc(n) for n in noise]).to(cuda_device))
+    torch.cuda.synchronize()
+    got = out.permute(0, 4, 1, 2, 3).cpu().numpy()
+    oracle = OracleUnet(torch_weights(raw, torch.float32), OracleConfig(16, 1, (4,), (1, 2, 4), 32, False))
+
+    def denoise(net_in, t, condition):
+        return oracle(torch.from_numpy(net_in), torch.from_numpy(t), torch.from_numpy(condition)).float().numpy()
+
+    coeffs = oracle_samplers.ddim_coefficients(alphas, steps)
+    want = oracle_samplers.ddim_sample(denoise, ctx, cond, coeffs, initial_noise=init, step_noise=list(noise))
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, want) <= 1e-4
+
+
 @pytest.mark.parametrize("quantize", [True, False])
 def test_vq_decoder_matches_reference_recording(cuda_device, quantize):
     from lesiondiffusion_mlx_b200.networks import VqDecoderB200

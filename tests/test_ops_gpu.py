@@ -198,7 +198,7 @@ def test_timestep_embedding_and_dense_small(cuda_device):
     assert np.all(np.abs(y.numpy() - ref.numpy()) <= ulp + 1e-3)
 
 
-def _ddim_on_gpu(device, f, toy):
+def _ddim_on_gpu(device, f, toy, eps_dtype=torch.float16):
     """Replay a reference DDIM recording with the fused GPU sampler step."""
     from lesiondiffusion_mlx_b200 import ops
 
@@ -224,7 +224,7 @@ def _ddim_on_gpu(device, f, toy):
         # network input as the reference builds it (f32 concat), then the toy denoiser
         net32 = torch.cat([x, m[..., None] if m is not None else img], dim=-1)
         eps = toy(ncdhw(net32).cpu().numpy(), np.array([t], np.int32), f["condition"])
-        eps_d = ndhwc(torch.from_numpy(np.asarray(eps, np.float32))).to(torch.float16).to(device)
+        eps_d = ndhwc(torch.from_numpy(np.asarray(eps, np.float32))).to(eps_dtype).to(device)
         ops.sampler_step(1, x, eps=eps_d, noise=noise, noise_step_stride=int(noise[0].numel()), mask=m,
                          image=img, net_in=net_in[..., : channels + extra], coeff=coeff, step=step)
         ops.step_advance(step)
@@ -242,6 +242,31 @@ def test_fused_ddim_step_replays_reference_trajectory(cuda_device, name):
     # toy denoiser's FP32 prediction rounds to f16 on the way in, so the
     # trajectory matches the recording to f16 input precision.
     np.testing.assert_allclose(got, f["output"], rtol=2e-3, atol=2e-3)
+
+
+def test_fused_ddim_step_fp32_prediction_replays_lmnet_trajectory(cuda_device):
+    """LMNet's sampler (no mask, [x | conditioning] input) with the FP32
+    network's f32 prediction: the recording at the reference's FP32
+    tolerance, and the next network input written in the split format."""
+    from lesiondiffusion_mlx_b200 import ops
+    from tests.golden.fixture_weights import sampling_toy_denoiser
+
+    f = golden("ddim_mask")
+    assert f.get("mask") is None
+    got = _ddim_on_gpu(cuda_device, f, sampling_toy_denoiser, eps_dtype=torch.float32)
+    np.testing.assert_allclose(got, f["output"], rtol=2e-5, atol=2e-6)
+    # split network input: hi + lo / 2048 reproduces [x | image] in FP32
+    x = ndhwc(torch.from_numpy(f["output"])).to(cuda_device).contiguous()
+    img = ndhwc(torch.from_numpy(f["image"])).to(cuda_device).contiguous()
+    c = int(x.shape[-1]) + int(img.shape[-1])
+    cpad = (c + 15) // 16 * 16
+    net = torch.full((*x.shape[:-1], 2 * cpad), 7.0, dtype=torch.float16, device=cuda_device)
+    ops.sampler_step(0, x, image=img, net_in=net, net_split=True)
+    torch.cuda.synchronize()
+    back = net[..., :cpad].float() + net[..., cpad:].float() / 2048.0
+    want = torch.cat([x, img], dim=-1)
+    assert torch.allclose(back[..., :c], want, rtol=1e-6, atol=1e-7)
+    assert torch.all(net[..., c:cpad] == 0) and torch.all(net[..., cpad + c:] == 0)
 
 
 @pytest.mark.parametrize("steps", [4, 8, 25])
