@@ -1119,6 +1119,15 @@ bool conv_trans_enabled() {
   return enabled;
 }
 
+// Tile-selection overrides for measurements (read on every plan): LDB_CONV_BN
+// (64 or 128) replaces the 256-column tile where the packed weight rows are
+// the same (out_channels a multiple of 256); LDB_CONV_SPLITS fixes the
+// split-K factor.  Unset or 0: the planner's choice.
+int env_int(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : 0;
+}
+
 struct ConvPlan {
   int kc, bn, taps, cin_pad, grid;
   ConvParams p;
@@ -1149,6 +1158,10 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   else if (cout <= 64) bn = 64;
   else if (cout <= 128 || exact) bn = 128;
   else bn = 256;
+  {
+    const int force_bn = env_int("LDB_CONV_BN");
+    if (bn == 256 && cout % 256 == 0 && (force_bn == 64 || force_bn == 128)) bn = force_bn;
+  }
   if (d->depth_halo < 0 || d->depth_halo > 1) return fail(LDB_ERR_SHAPE, "depth_halo must be 0 or 1");
   const bool stride2 = d->mode == LDB_CONV_3X3X3_S2 || d->mode == LDB_CONV_3X3X3_S2_PAD01;
   if (d->depth_halo && stride2) return fail(LDB_ERR_SHAPE, "depth_halo with stride 2");
@@ -1188,14 +1201,39 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
       static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
   if (out_tiles > (1LL << 30)) return fail(LDB_ERR_SHAPE, "conv has too many tiles");
   const int sms = sm_count();
+  const int force_bn = env_int("LDB_CONV_BN");
+  if (taps == 1 && !exact && bn == 256 && cout % 256 == 0 && force_bn == 0) {
+    // Pointwise: K is a few k-blocks, so split-K would only add a reduce
+    // pass; fill the SMs with narrower column tiles instead.  Cost per tile
+    // = k-blocks x shared-memory-bound k-block time ((128 + BN) x KC / 32
+    // cycles: TMA writes plus MMA operand reads) + ~4000 cycles of set-up and
+    // epilogue, times the waves of the persistent grid.
+    const long long m_tiles = out_tiles / p.n_tiles;
+    long long best = -1;
+    for (int cand : {256, 128, 64}) {
+      const long long tiles = m_tiles * (cout / cand);
+      const long long cost = ((tiles + sms - 1) / sms) * (static_cast<long long>(p.kb_total) * (128 + cand) * kc / 32 + 4000);
+      if (best < 0 || cost < best) {
+        best = cost;
+        bn = cand;
+      }
+    }
+    p.n_tiles = (cout + bn - 1) / bn;
+    p.wrows_per_parity = p.n_tiles * bn;
+  }
+  const long long tiles_now = static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
   int splits = 1;
-  if (out_tiles < sms && p.kb_total >= 8) {
-    splits = static_cast<int>(std::min<long long>(sms / out_tiles, p.kb_total / 4));
+  if (taps > 1 && tiles_now < sms && p.kb_total >= 8) {
+    splits = static_cast<int>(std::min<long long>(sms / tiles_now, p.kb_total / 4));
     splits = std::max(1, splits);
+  }
+  {
+    const int force_splits = env_int("LDB_CONV_SPLITS");
+    if (force_splits > 0) splits = std::min(force_splits, p.kb_total);
   }
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
-  p.num_tiles = static_cast<int>(out_tiles * p.k_splits);
+  p.num_tiles = static_cast<int>(tiles_now * p.k_splits);
   p.cout = cout;
   p.out_ld = d->out_ld;
   p.res_ld = d->res_ld;
