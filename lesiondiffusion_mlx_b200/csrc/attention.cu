@@ -71,6 +71,33 @@ struct AttnCfg {
   static_assert(kSmemBytes <= 232448, "attention shared memory");
 };
 
+// Paired FP32 arithmetic (sm_100 f32x2 instructions) and the 3-input max:
+// the softmax issues one instruction per pair of scores for the scale and
+// the row sum, and one per two scores for the row maximum.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 struct AttnParams {
   int batch, heads, lq, lk;
   int out_ld;        // elements between output rows
@@ -279,16 +306,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < kBlockN; ++i)
           if (i >= valid) sr[i] = __float_as_uint(-INFINITY);
       }
-      // row maximum as 8 independent chains folded by a tree
-      float m8[8];
+      // row maximum: four independent chains of 3-input maxima, folded
+      float m4[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(sr[k]);
+      for (int k = 0; k < 4; ++k) m4[k] = fmaxf(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
 #pragma unroll
       for (int i = 8; i < kBlockN; i += 8)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(sr[i + k]));
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int k = 0; k < 4; ++k)
+          m4[k] = max3(m4[k], __uint_as_float(sr[i + 2 * k]), __uint_as_float(sr[i + 2 * k + 1]));
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const bool first = j == 0;
       const bool grow = first || (mx - m_ref) * c > kRescaleLog2;
       const float m_new = grow ? fmaxf(m_ref, mx) : m_ref;
@@ -320,16 +347,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_ref = m_new;
       }
       const float mc = m_ref * c;
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+      const uint64_t c2 = pack2(c, c), nmc2 = pack2(-mc, -mc);
+      uint64_t sum2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};  // independent paired row sums
 #pragma unroll
       for (int c0 = 0; c0 < kBlockN; c0 += 32) {
         uint32_t packed[16];
         uint32_t packed_lo[SPLIT ? 16 : 1];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c0 + i]), c, -mc));
-          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c0 + i + 1]), c, -mc));
-          s4[(i >> 1) & 3] += e0 + e1;
+          float x0, x1;
+          unpack2(fma2(pack2(__uint_as_float(sr[c0 + i]), __uint_as_float(sr[c0 + i + 1])), c2, nmc2), x0, x1);
+          const float e0 = ex2_approx(x0);
+          const float e1 = ex2_approx(x1);
+          sum2[(i >> 1) & 1] = add2(sum2[(i >> 1) & 1], pack2(e0, e1));
           if constexpr (BF16) {
             __nv_bfloat162 v2 = __floats2bfloat162_rn(e0, e1);
             packed[i / 2] = *reinterpret_cast<uint32_t*>(&v2);
@@ -348,7 +378,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_st16(tmem_s + (c0 >> 1), packed);
         if constexpr (SPLIT) tmem_st16(tmem_s + 64 + (c0 >> 1), packed_lo);
       }
-      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      {
+        float a0, a1, b0, b1;
+        unpack2(sum2[0], a0, a1);
+        unpack2(sum2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
