@@ -355,7 +355,18 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, uint32_t ab_
 
 // ---------------------------------------------------------------- misc
 
-__device__ __forceinline__ float silu_f32(float y) { return y / (1.0f + expf(-y)); }
+// SiLU y * sigmoid(y) with the sigmoid from the hardware ex2 and reciprocal
+// approximations (relative error ~3e-7, far below the f16 rounding that
+// follows and the FP32 network's 1e-4 tolerance): two special-function
+// operations instead of a full-precision expf and an IEEE division.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float silu_f32(float y) {
+  return y * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * y));
+}
 
 __device__ __forceinline__ float gelu_erf_f32(float y) {
   return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f));

@@ -217,65 +217,100 @@ __global__ void gn_finalize_kernel(Src2 s, int voxels, const float2* partials, i
 // out = prepare(x): optional affine (scale, offset per channel) and SiLU in
 // FP32, then either one f16 rounding or the exact split into hi / 2^11-scaled
 // lo planes (_nax_conv.py:109-155).  Channels past C up to the padded plane
-// width are written as zeros.  One call per 8 channels of one voxel; `aff`
-// points at the (scale, offset) pairs of channels c .. c + 7 (global or
-// shared memory) or is null.
-__device__ __forceinline__ void prepare_vec(const Src2& s, long long voxel, int c, const float* aff, int silu,
-                                            int split, int cpad, __half* out, int out_ld) {
-  const int c_total = s.c1 + s.c2;
-  float v[8];
-  if (c + 8 <= c_total) {
-    load8(s, voxel, c, v);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = 0.f;
-  }
-  uint4 hi_raw, lo_raw;
-  __half* hi = reinterpret_cast<__half*>(&hi_raw);
-  __half* lo = reinterpret_cast<__half*>(&lo_raw);
+// width are written as zeros.
+//
+// Each thread owns one 8-channel group c of one batch item for the whole
+// pass: its 8 (scale, offset) pairs stay in registers and it walks voxels
+// with a stride, four voxels' loads in flight before their stores.  Blocks
+// are a whole number of channel-group rows (blockDim = rows x cpad / 8).
+struct Affine8 {
   float sc[8], of[8];
-  const bool affine = aff != nullptr && c + 8 <= c_total;
-  if (affine) {
-    // 8 (scale, offset) pairs = four 16-byte loads
+  bool on;
+};
+
+__device__ __forceinline__ Affine8 load_affine8(const float* aff, int c, int c_total) {
+  Affine8 a;
+  a.on = aff != nullptr && c + 8 <= c_total;
+  if (a.on) {
     const float4* a4 = reinterpret_cast<const float4*>(aff);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float4 t = a4[q];
-      sc[2 * q] = t.x;
-      of[2 * q] = t.y;
-      sc[2 * q + 1] = t.z;
-      of[2 * q + 1] = t.w;
+      a.sc[2 * q] = t.x;
+      a.of[2 * q] = t.y;
+      a.sc[2 * q + 1] = t.z;
+      a.of[2 * q + 1] = t.w;
     }
   }
+  return a;
+}
+
+__device__ __forceinline__ void prepare_store(const float (&v)[8], int c, int c_total, const Affine8& a, int silu,
+                                              int split, int cpad, __half* o) {
+  uint4 hi_raw, lo_raw;
+  __half* hi = reinterpret_cast<__half*>(&hi_raw);
+  __half* lo = reinterpret_cast<__half*>(&lo_raw);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float y = 0.f;
     if (c + j < c_total) {
       y = v[j];
-      if (affine) y = fmaf(y, sc[j], of[j]);
+      if (a.on) y = fmaf(y, a.sc[j], a.of[j]);
       if (silu) y = silu_f32(y);
     }
     hi[j] = __float2half_rn(y);
     if (split) lo[j] = __float2half_rn((y - __half2float(hi[j])) * 2048.0f);
   }
-  __half* o = out + voxel * out_ld + c;
   *reinterpret_cast<uint4*>(o) = hi_raw;
   if (split) *reinterpret_cast<uint4*>(o + cpad) = lo_raw;
 }
 
-// One thread per 8 channels of one voxel; `affine` is (B, C, 2) or null.
-__global__ void prepare_kernel(Src2 s, long long voxels_total, int voxels_per_batch, const float* affine, int silu,
-                               int split, int cpad, __half* out, int out_ld) {
-  pdl_begin();
+// Voxels [0, voxels) of the batch item starting at global voxel v0.
+__device__ __forceinline__ void prepare_pass(const Src2& s, long long v0, int voxels, const Affine8& a, int c,
+                                             int silu, int split, int cpad, __half* out, int out_ld) {
   const int c_total = s.c1 + s.c2;
   const int vecs = cpad / 8;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= voxels_total * vecs) return;
-  const long long voxel = idx / vecs;
-  const int c = static_cast<int>(idx % vecs) * 8;
-  const int b = static_cast<int>(voxel / voxels_per_batch);
-  const float* aff = affine ? affine + (static_cast<long long>(b) * c_total + c) * 2 : nullptr;
-  prepare_vec(s, voxel, c, aff, silu, split, cpad, out, out_ld);
+  const int rows = blockDim.x / vecs;
+  const long long stride = static_cast<long long>(gridDim.x) * rows;
+  const bool live = c + 8 <= c_total;
+  long long v = static_cast<long long>(blockIdx.x) * rows + threadIdx.x / vecs;
+  for (; v + 3 * stride < voxels; v += 4 * stride) {
+    float x[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (live) {
+        load8(s, v0 + v + u * stride, c, x[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[u][j] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      prepare_store(x[u], c, c_total, a, silu, split, cpad, out + (v0 + v + u * stride) * out_ld + c);
+  }
+  for (; v < voxels; v += stride) {
+    float x[8];
+    if (live) {
+      load8(s, v0 + v, c, x);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = 0.f;
+    }
+    prepare_store(x, c, c_total, a, silu, split, cpad, out + (v0 + v) * out_ld + c);
+  }
+}
+
+// Block (x, b): batch item b; `affine` is (B, C, 2) or null.
+__global__ void prepare_kernel(Src2 s, int voxels_per_batch, const float* affine, int silu, int split, int cpad,
+                               __half* out, int out_ld) {
+  pdl_begin();
+  const int c_total = s.c1 + s.c2;
+  const int c = (threadIdx.x % (cpad / 8)) * 8;
+  const int b = blockIdx.y;
+  const Affine8 a = load_affine8(affine ? affine + (static_cast<long long>(b) * c_total + c) * 2 : nullptr, c, c_total);
+  prepare_pass(s, static_cast<long long>(b) * voxels_per_batch, voxels_per_batch, a, c, silu, split, cpad, out,
+               out_ld);
 }
 
 // GroupNorm affine of batch item b from producer statistics (per channel FP64
@@ -357,7 +392,7 @@ __global__ void gn_stats_affine_kernel(const double* st1, int c1, const double* 
 // GroupNorm from producer statistics fused with the normalize pass: block
 // (x, b) derives the affine of batch item b into shared memory (the same
 // arithmetic as gn_stats_affine_kernel, so the same bits), then applies it
-// with prepare_vec over a grid-stride range of b's voxels.
+// with prepare_pass over a strided range of b's voxels.
 __global__ void prepare_stats_kernel(Src2 s, int voxels, int stat_voxels, const double* st1, const double* st2,
                                      int groups, const float* gamma, const float* beta, float eps, int silu,
                                      int split, int cpad, __half* out, int out_ld) {
@@ -370,15 +405,9 @@ __global__ void prepare_stats_kernel(Src2 s, int voxels, int stat_voxels, const 
   stage_gamma_beta(gamma, beta, C, aff);
   pdl_begin();
   block_affine_from_stats(st1, s.c1, st2, s.c2, b, groups, stat_voxels, eps, aff, sts, gm);
-  const int vecs = cpad / 8;
-  const long long total = static_cast<long long>(voxels) * vecs;
-  const long long v0 = static_cast<long long>(b) * voxels;
-  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long vox = idx / vecs;
-    const int c = static_cast<int>(idx - vox * vecs) * 8;
-    prepare_vec(s, v0 + vox, c, c < C ? aff + c * 2 : nullptr, silu, split, cpad, out, out_ld);
-  }
+  const int c = (threadIdx.x % (cpad / 8)) * 8;
+  const Affine8 a = load_affine8(c < C ? aff + c * 2 : nullptr, c, C);
+  prepare_pass(s, static_cast<long long>(b) * voxels, voxels, a, c, silu, split, cpad, out, out_ld);
 }
 
 // LayerNorm over the last axis of (rows, C) f16 (mlx_model.py:360-367):
@@ -478,6 +507,21 @@ int make_src(const void* x1, int c1, int ld1, const void* x2, int c2, int ld2, i
 
 // Kernels whose shared memory grows with the channel count may need more
 // than the default 48 KB (at most 4096 channels: 97 KB plus the groups).
+// Threads per block of the normalize pass: whole rows of cpad / 8 channel
+// groups, about 256 threads; and the blocks per batch item (about 8 blocks of
+// 256 threads per SM over the batch, at most one row pass per voxel).
+int prepare_threads(int cpad) {
+  const int vecs = cpad / 8;
+  return vecs >= 256 ? vecs : (256 / vecs) * vecs;
+}
+
+int prepare_blocks(int cpad, int voxels, int batch) {
+  const int rows = prepare_threads(cpad) / (cpad / 8);
+  const long long want = (static_cast<long long>(voxels) + rows - 1) / rows;
+  const long long cap = std::max(1, (8 * sm_count() * 256) / (prepare_threads(cpad) * batch));
+  return static_cast<int>(std::max<long long>(1, std::min(want, cap)));
+}
+
 int stats_smem_attribute(const void* kernel, size_t bytes, unsigned long long* configured) {
   if (bytes <= 48 * 1024) return LDB_OK;
   return ensure_smem_attribute(kernel, 100 * 1024, configured, "stats smem attribute");
@@ -587,12 +631,11 @@ int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, cons
   const int cpad = split ? ((C + 15) / 16) * 16 : ((C + 7) / 8) * 8;
   if (out_ld % 8 || out_ld < (split ? 2 * cpad : cpad))
     return fail(LDB_ERR_ALIGNMENT, "out_ld %d too small or not a multiple of 8", out_ld);
-  const long long total = static_cast<long long>(batch) * voxels * (cpad / 8);
-  if (total <= 0) return fail(LDB_ERR_SHAPE, "empty input");
-  const int threads = 256;
-  return launch_kernel(prepare_kernel, dim3(static_cast<unsigned>((total + threads - 1) / threads)), dim3(threads),
-                       0, stream, "prepare launch", s, static_cast<long long>(batch) * voxels, voxels, affine, silu,
-                       split, cpad, static_cast<__half*>(out), out_ld);
+  if (batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "empty input");
+  if (cpad / 8 > 1024) return fail(LDB_ERR_SHAPE, "at most 8192 channels");
+  return launch_kernel(prepare_kernel, dim3(static_cast<unsigned>(prepare_blocks(cpad, voxels, batch)), batch),
+                       dim3(prepare_threads(cpad)), 0, stream, "prepare launch", s, voxels, affine, silu, split, cpad,
+                       static_cast<__half*>(out), out_ld);
 }
 
 int ldb_group_norm_affine_from_stats(cudaStream_t stream, const double* stats1, int c1, const double* stats2,
@@ -633,12 +676,8 @@ int ldb_prepare_input_from_stats(cudaStream_t stream, const void* x1, int c1, in
   static unsigned long long configured = 0;
   rc = stats_smem_attribute(reinterpret_cast<const void*>(prepare_stats_kernel), smem, &configured);
   if (rc != LDB_OK) return rc;
-  const int threads = 256;
-  const long long per_batch = static_cast<long long>(voxels) * (cpad / 8);
-  // About 8 blocks of 256 threads per SM over the whole batch.
-  const long long cap = std::max(1, (8 * sm_count()) / batch);
-  const long long blocks = std::min((per_batch + threads - 1) / threads, cap);
-  return launch_kernel(prepare_stats_kernel, dim3(static_cast<unsigned>(blocks), batch), dim3(threads), smem,
+  return launch_kernel(prepare_stats_kernel, dim3(static_cast<unsigned>(prepare_blocks(cpad, voxels, batch)), batch),
+                       dim3(prepare_threads(cpad)), smem,
                        stream, "prepare from stats launch", s, voxels, stat_voxels, stats1, s.c2 > 0 ? stats2 : stats1, groups,
                        gamma, beta, eps, silu, split, cpad, static_cast<__half*>(out), out_ld);
 }
