@@ -234,9 +234,13 @@ def main() -> None:
     prepared.begin(init, noise)
 
     # Capture one step (UNet + DDIM update + step advance) twice: a plain graph
-    # for the timed region, and a copy with per-kernel event records (whose
-    # event nodes add gaps) replayed afterwards for the per-kernel breakdown.
-    timer = instrument.KernelTimer()
+    # for the timed region, and a copy replayed afterwards for the per-kernel
+    # breakdown.  In the copy every conv launch times itself from the device
+    # clock (its first CTA past the dependency wait to its last CTA or split-K
+    # reduce finishing; no node is added to its path), and the other kernels
+    # have CUDA event pairs around them (whose nodes add gaps).
+    timer = instrument.KernelTimer(device_clock=True)
+    timer.arm(device)
     prepared._step()  # eager warm-up (first-use setup outside capture)
     torch.cuda.synchronize()
     launches0 = _lib.launch_count()
@@ -286,6 +290,7 @@ def main() -> None:
     elapsed_ms = start.elapsed_time(end)
     prepared.begin(init, noise)
     for _ in range(3):
+        timer.reset()
         timed_graph.replay()
     torch.cuda.synchronize()
     kernel = timer.summary()

@@ -109,6 +109,13 @@ typedef struct {
    * interior slices (twice that for LDB_CONV_UP2).  0 or 1; not with stride 2 (modes 1 and 4).
    * Used by the depth-sharded decode, where each GPU holds a slab. */
   int depth_halo;
+  /* Optional device pointer to two 64-bit words (start, end) for timing the
+   * launch from the device clock (%globaltimer, ns): the kernel lowers start
+   * (atomic min) to the time its first CTA passes its dependency wait and
+   * raises end (atomic max) to the time its last CTA, or the split-K reduce,
+   * finishes.  The caller sets start high and end to 0 before the launch.
+   * Null: no timing. */
+  unsigned long long* clock;
 } ldb_conv_desc;
 
 /* Workspace bytes ldb_conv3d_fwd needs (split-K partial tiles; 0 if none). */
@@ -245,6 +252,15 @@ LDB_API int ldb_flash_attention_f32(ldb_stream_t stream, const float* q, int q_l
                                     int head_dim, float scale, void* workspace, size_t workspace_bytes);
 
 LDB_API int ldb_flash_attention_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes);
+/* ldb_flash_attention_ws timed from the device clock: `clock` (device, two
+ * 64-bit words set high / 0 by the caller) receives the time the first CTA
+ * passes its dependency wait (atomic min) and the time the last CTA or the
+ * key-split merge finishes (atomic max), in ns of %globaltimer.  For
+ * benchmarks; results are those of ldb_flash_attention_ws. */
+LDB_API int ldb_flash_attention_timed(ldb_stream_t stream, const void* q, int q_ld, const void* k, const void* v,
+                                      int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads,
+                                      int head_dim, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                      unsigned long long* clock);
 LDB_API int ldb_flash_attention_ws(ldb_stream_t stream, const void* q, int q_ld, const void* k, const void* v,
                                    int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads,
                                    int head_dim, float scale, int dtype, void* workspace, size_t workspace_bytes);

@@ -47,6 +47,7 @@ class ConvDesc(ctypes.Structure):
         ("act", ctypes.c_int),
         ("output_scale", ctypes.c_float),
         ("depth_halo", ctypes.c_int),
+        ("clock", ctypes.c_void_p),
     ]
 
 
@@ -77,6 +78,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_flash_attention_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],
     "ldb_flash_attention_f32_workspace_size": [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)],
     "ldb_flash_attention_f32": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _P, _SZ],
+    "ldb_flash_attention_timed": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P],
     "ldb_flash_attention_ws": [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _SZ],
     "ldb_step_advance": [_P, _P],
     "ldb_timestep_embedding": [_P, _P, _P, _I, _I, _P, _I],

@@ -275,7 +275,8 @@ def conv3d_ndhwc(
     if stats is not None and (stats.dtype != torch.float64 or tuple(stats.shape) != (batch, cout, 2)
                               or not stats.is_contiguous()):
         raise ValueError(f"stats must be a contiguous float64 {(batch, cout, 2)} tensor")
-    with instrument.maybe_time("conv3d", flops):
+    desc.clock = instrument.device_clock("conv3d", flops, x.device)
+    with instrument.maybe_time("conv3d", flops, device_clocked=desc.clock is not None):
         if stats is None:
             _lib.call(
                 "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),

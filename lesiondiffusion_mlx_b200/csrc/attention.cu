@@ -110,6 +110,9 @@ struct AttnParams {
   int kv_splits, blocks_per_split;
   float* o_part;
   float* ml_part;
+  // Device-clock timing of the launch (may be null): [start, end] in ns,
+  // lowered / raised atomically by the CTAs (and the merge kernel).
+  unsigned long long* clock;
 };
 
 template <int D, bool BF16, bool SPLIT>
@@ -171,6 +174,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_begin();
+  if (p.clock && threadIdx.x == 0) atomicMin(p.clock, static_cast<unsigned long long>(globaltimer_ns()));
 
   // The register split sits at the top of each warpgroup's branch (one
   // instruction for all four warps), so every role's code is compiled with
@@ -471,6 +475,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+  if (p.clock && threadIdx.x == 0) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
 }
 
 // Merge the key splits of each query row: M = max of the splits' reference
@@ -503,6 +508,7 @@ __global__ void attn_combine_kernel(const AttnParams p) {
   T* out = static_cast<T*>(p.out) + (static_cast<long long>(b) * p.lq + q) * p.out_ld + h * D;
   if (lane < D) out[lane] = static_cast<T>(a0 * inv);
   if (lane + 32 < D) out[lane + 32] = static_cast<T>(a1 * inv);
+  if (p.clock && lane == 0) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
 }
 
 // FP32 projections -> split f16 planes for the SPLIT kernel.  src is
@@ -588,7 +594,8 @@ extern "C" {
 
 static int flash_attention_impl(cudaStream_t stream, const void* q, int q_ld, const void* k, const void* v,
                                 int kv_ld, void* out, int out_ld, int batch, int lq, int lk, int heads,
-                                int head_dim, float scale, int dtype, void* workspace, size_t workspace_bytes) {
+                                int head_dim, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                unsigned long long* clock) {
   using namespace ldb;
   if (!q || !k || !v || !out) return fail(LDB_ERR_INVALID, "flash_attention: null pointer");
   if (head_dim != 16 && head_dim != 32 && head_dim != 64)
@@ -626,6 +633,7 @@ static int flash_attention_impl(cudaStream_t stream, const void* q, int q_ld, co
   p.out_ld = out_ld;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out;
+  p.clock = clock;
   const int blocks = (lk + kBlockN - 1) / kBlockN;
   const long long ctas = static_cast<long long>((lq + 2 * kBlockM - 1) / (2 * kBlockM)) * heads * batch;
   p.kv_splits = 1;
@@ -651,7 +659,7 @@ int ldb_flash_attention(cudaStream_t stream, const void* q, int q_ld, const void
                         void* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim, float scale,
                         int dtype) {
   return flash_attention_impl(stream, q, q_ld, k, v, kv_ld, out, out_ld, batch, lq, lk, heads, head_dim, scale, dtype,
-                              nullptr, 0);
+                              nullptr, 0, nullptr);
 }
 
 int ldb_flash_attention_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes) {
@@ -670,7 +678,14 @@ int ldb_flash_attention_ws(cudaStream_t stream, const void* q, int q_ld, const v
                            void* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim, float scale,
                            int dtype, void* workspace, size_t workspace_bytes) {
   return flash_attention_impl(stream, q, q_ld, k, v, kv_ld, out, out_ld, batch, lq, lk, heads, head_dim, scale, dtype,
-                              workspace, workspace_bytes);
+                              workspace, workspace_bytes, nullptr);
+}
+
+int ldb_flash_attention_timed(cudaStream_t stream, const void* q, int q_ld, const void* k, const void* v, int kv_ld,
+                              void* out, int out_ld, int batch, int lq, int lk, int heads, int head_dim, float scale,
+                              int dtype, void* workspace, size_t workspace_bytes, unsigned long long* clock) {
+  return flash_attention_impl(stream, q, q_ld, k, v, kv_ld, out, out_ld, batch, lq, lk, heads, head_dim, scale, dtype,
+                              workspace, workspace_bytes, clock);
 }
 
 int ldb_flash_attention_f32_workspace_size(int batch, int lq, int lk, int heads, int head_dim, size_t* bytes) {
@@ -750,6 +765,7 @@ int ldb_flash_attention_f32(cudaStream_t stream, const float* q, int q_ld, const
   p.kv_splits = 1;
   p.blocks_per_split = (lk + kBlockN - 1) / kBlockN;
   p.o_part = p.ml_part = nullptr;
+  p.clock = nullptr;
   if (head_dim == 64) return launch_attn<64, false, true>(stream, qm, km, vm, p);
   if (head_dim == 16) return launch_attn<16, false, true>(stream, qm, km, vm, p);
   return launch_attn<32, false, true>(stream, qm, km, vm, p);

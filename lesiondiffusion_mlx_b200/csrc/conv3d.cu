@@ -788,6 +788,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           if (!waited) {
             pdl_wait();
             waited = true;
+            if (p.clock) atomicMin(p.clock, static_cast<unsigned long long>(globaltimer_ns()));
           }
           tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
           tma_load_2d(sb, &wmap, &full[stage], tap * p.cin_pad + chn, brow);
@@ -911,7 +912,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       named_barrier(1, 128);
       flush_stats<BN>(p, st, false);
     }
-    if (st.leader) bulk_wait_group_all();  // stores must finish before the CTA releases its shared memory
+    if (st.leader) {
+      bulk_wait_group_all();  // stores must finish before the CTA releases its shared memory
+      if (p.clock && !split) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
+    }
   }
 
   __syncwarp();
@@ -985,7 +989,10 @@ __global__ void __launch_bounds__(256) conv_reduce_kernel(const ConvParams p) {
     nvalid += voxel >= 0;
     if (live[i]) store_outputs<4>(p, c.b, voxel, col, v[i]);
   }
-  if (!stats) return;
+  if (!stats) {
+    if (p.clock && threadIdx.x == 0) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
+    return;
+  }
   float k[4], d1[4], d2[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -1034,6 +1041,7 @@ __global__ void __launch_bounds__(256) conv_reduce_kernel(const ConvParams p) {
       red_add_f64(dst + 1, s2 + 2.0 * kk * s1 + n * kk * kk);
     }
   }
+  if (p.clock && threadIdx.x == 0) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
 }
 
 // Brick of at most 128 voxels covering a (d, h, w) grid with the fewest
@@ -1331,6 +1339,7 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
   p.residual = residual;
   p.out = out;
   p.stats = stats;
+  p.clock = desc->clock;
   p.partials = static_cast<float*>(workspace);
 
   const int B = desc->batch, D = desc->depth, H = desc->height, W = desc->width;

@@ -59,6 +59,8 @@ struct ConvParams {
   // channel) the FP64 sum and sum of squares, added atomically.
   double* stats;
   int out_d, out_h, out_w;
+  // Device-clock timing of the launch (may be null): [start, end] in ns.
+  unsigned long long* clock;
 };
 
 // Tensor maps of one convolution: activation loads (one map, or 8 parity

@@ -210,11 +210,13 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
     ws_bytes = ctypes.c_size_t(0)
     _lib.call("ldb_flash_attention_workspace_size", batch, lq, lk, heads, width // heads, ctypes.byref(ws_bytes))
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=q.device) if ws_bytes.value else None
-    with instrument.maybe_time("attention", 4.0 * batch * lq * lk * width):
+    flops = 4.0 * batch * lq * lk * width
+    clock = instrument.device_clock("attention", flops, q.device)
+    with instrument.maybe_time("attention", flops, device_clocked=clock is not None):
         _lib.call(
-            "ldb_flash_attention_ws", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
+            "ldb_flash_attention_timed", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
             int(k.stride(1)), out.data_ptr(), int(out.stride(1)), batch, lq, lk, heads, width // heads,
-            float(scale), _DT[q.dtype], _ptr(ws), ws_bytes.value,
+            float(scale), _DT[q.dtype], _ptr(ws), ws_bytes.value, clock,
         )
     return out
 
