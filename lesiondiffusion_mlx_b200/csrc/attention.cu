@@ -21,6 +21,7 @@
 // partial block).
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -33,11 +34,11 @@ namespace {
 // WG2 = the softmax of query tiles 0 and 1.  Ten or twelve warps put three
 // warps on some SM sub-partitions, which caps a thread at 168 registers at
 // launch; WG0 gives registers up (setmaxnreg) so the softmax warps, which
-// hold a 128-score row each, get 224.  128 x 56 + 256 x 224 = 384 x 168.
+// hold a 128-score row each, get 216.  128 x 72 + 256 x 216 = 384 x 168.
 constexpr int kAttnThreads = 384;
 constexpr int kAttnLaunchRegs = 168;
-constexpr int kAttnRegsWg0 = 56;
-constexpr int kAttnRegsSoftmax = 224;
+constexpr int kAttnRegsWg0 = 72;
+constexpr int kAttnRegsSoftmax = 216;
 static_assert(128 * kAttnRegsWg0 + 256 * kAttnRegsSoftmax <= kAttnThreads * kAttnLaunchRegs, "register split");
 constexpr int kBlockM = 128;       // queries per tile (two tiles per CTA)
 constexpr int kBlockN = 128;       // keys per block
@@ -63,7 +64,7 @@ struct AttnCfg {
   static constexpr int kStageBytes = 2 * kPlanes * kKBytes;
   static constexpr int kOffBar = kOffK + kStages * kStageBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers: 2 kStages + 8 words, then the TMEM slot
-  static_assert((2 * kStages + 8) * 8 + 16 <= 256, "attention barrier block");
+  static_assert((2 * kStages + 9) * 8 + 16 <= 256, "attention barrier block");
   // TMEM: S0 [0,128), S1 [128,256), O0 [256, 256 + planes*D), O1 [384, 384 + planes*D).
   // The probabilities overwrite their scores as packed 16-bit pairs: P_t
   // plane 0 in columns [128t, 128t + 64), plane 1 in [128t + 64, 128t + 128).
@@ -113,7 +114,72 @@ struct AttnParams {
   // Device-clock timing of the launch (may be null): [start, end] in ns,
   // lowered / raised atomically by the CTAs (and the merge kernel).
   unsigned long long* clock;
+  // Stream-K schedule (sk_ctas > 0; blockIdx.x = CTA, grid 1 x 1 in y, z):
+  // the sk_units = pairs x sk_nb (query pair, key block) units are cut into
+  // sk_ctas equal ranges; sk_pairs query pairs per (batch, head); a CTA's
+  // segment s of a pair it does not cover whole writes its raw O rows and
+  // (reference max, sum) to slot blockIdx.x * sk_slots + s of o_part /
+  // ml_part (256 rows each) for attn_sk_merge_kernel.
+  int sk_ctas, sk_nb, sk_pairs, sk_slots;
+  long long sk_units;
 };
+
+// One segment of a CTA's work: a query pair (two 128-row tiles of one batch
+// item and head) over a range of key blocks.  The plain schedule has one
+// segment per CTA (its pair, all keys or one key split); the stream-K
+// schedule gives a CTA the end of one pair and the start of the next (or a
+// few pairs), each a segment, so every CTA does the same number of blocks.
+struct AttnSeg {
+  int b, h, q0, jb0, nblocks;
+  bool whole;
+};
+
+struct AttnSched {
+  long long u, u_end;
+};
+
+__device__ __forceinline__ long long sk_unit0(const AttnParams& p, long long cta) {
+  return cta * p.sk_units / p.sk_ctas;
+}
+
+__device__ __forceinline__ AttnSched sched_begin(const AttnParams& p) {
+  AttnSched sc;
+  if (p.sk_ctas > 0) {
+    sc.u = sk_unit0(p, blockIdx.x);
+    sc.u_end = sk_unit0(p, blockIdx.x + 1);
+  } else {
+    sc.u = 0;
+    sc.u_end = 1;
+  }
+  return sc;
+}
+
+__device__ __forceinline__ bool sched_next(const AttnParams& p, AttnSched& sc, AttnSeg& g) {
+  if (sc.u >= sc.u_end) return false;
+  if (p.sk_ctas > 0) {
+    const long long pair = sc.u / p.sk_nb;
+    const int j0 = static_cast<int>(sc.u - pair * p.sk_nb);
+    const int n = static_cast<int>(min(static_cast<long long>(p.sk_nb - j0), sc.u_end - sc.u));
+    const long long bh = pair / p.sk_pairs;
+    g.q0 = static_cast<int>(pair - bh * p.sk_pairs) * 2 * kBlockM;
+    g.h = static_cast<int>(bh % p.heads);
+    g.b = static_cast<int>(bh / p.heads);
+    g.jb0 = j0;
+    g.nblocks = n;
+    g.whole = j0 == 0 && n == p.sk_nb;
+    sc.u += n;
+  } else {
+    const int split = blockIdx.x % p.kv_splits;
+    g.q0 = (blockIdx.x / p.kv_splits) * 2 * kBlockM;
+    g.h = blockIdx.y;
+    g.b = blockIdx.z;
+    g.jb0 = split * p.blocks_per_split;
+    g.nblocks = min((p.lk + kBlockN - 1) / kBlockN - g.jb0, p.blocks_per_split);
+    g.whole = p.kv_splits == 1;
+    sc.u = sc.u_end;
+  }
+  return true;
+}
 
 template <int D, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -133,17 +199,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* p_ready = s_full + 2;           // [2]
   uint64_t* pv_done = p_ready + 2;          // [2]
   uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* q_empty = drain + 1;            // the S MMAs of a segment have read Q
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int split = blockIdx.x % p.kv_splits;
-  const int q0 = (blockIdx.x / p.kv_splits) * 2 * kBlockM;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int jb0 = split * p.blocks_per_split;  // first key block of this CTA
-  const int nblocks = min((p.lk + kBlockN - 1) / kBlockN - jb0, p.blocks_per_split);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -157,6 +218,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&pv_done[t], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(q_empty, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -185,28 +247,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t armed_mask = 0, armed_parity = 0;
-      mbar_arrive_expect_tx(q_full, 2 * kPl * Cfg::kQBytes);
-      // head h, plane pl starts at column (h * planes + pl) * D of the projection row
-      for (int t = 0; t < 2; ++t)
-        for (int pl = 0; pl < kPl; ++pl)
-          tma_load_3d(smem + (t * kPl + pl) * Cfg::kQBytes, &qmap, q_full, (h * kPl + pl) * D, q0 + t * kBlockM, b);
-      for (int j = 0; j < nblocks; ++j) {
-        const int st = j % Cfg::kStages;
-        const uint32_t ph = (j / Cfg::kStages) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status)) break;
-        uint8_t* sk = smem + Cfg::kOffK + st * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&kv_full[st], Cfg::kStageBytes);
-        armed_mask |= 1u << st;
-        armed_parity = (armed_parity & ~(1u << st)) | (ph << st);
-        for (int pl = 0; pl < kPl; ++pl) {
-          tma_load_3d(sk + pl * Cfg::kKBytes, &kmap, &kv_full[st], (h * kPl + pl) * D, (jb0 + j) * kBlockN, b);
-          tma_load_3d(sk + (kPl + pl) * Cfg::kKBytes, &vmap, &kv_full[st], (h * kPl + pl) * D,
-                      (jb0 + j) * kBlockN, b);
+      AttnSched sc = sched_begin(p);
+      AttnSeg g;
+      long long blk = 0;  // key blocks loaded so far (the K/V ring position)
+      int qloads = 0;
+      bool ok = true;
+      while (ok && sched_next(p, sc, g)) {
+        // the previous segment's S MMAs must have read the Q buffer
+        if (qloads > 0 && !mbar_wait(q_empty, (qloads - 1) & 1, abort_flag, status)) break;
+        mbar_arrive_expect_tx(q_full, 2 * kPl * Cfg::kQBytes);
+        // head h, plane pl starts at column (h * planes + pl) * D of the projection row
+        for (int t = 0; t < 2; ++t)
+          for (int pl = 0; pl < kPl; ++pl)
+            tma_load_3d(smem + (t * kPl + pl) * Cfg::kQBytes, &qmap, q_full, (g.h * kPl + pl) * D,
+                        g.q0 + t * kBlockM, g.b);
+        ++qloads;
+        for (int j = 0; j < g.nblocks; ++j, ++blk) {
+          const int st = static_cast<int>(blk % Cfg::kStages);
+          const uint32_t ph = static_cast<uint32_t>(blk / Cfg::kStages) & 1u;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sk = smem + Cfg::kOffK + st * Cfg::kStageBytes;
+          mbar_arrive_expect_tx(&kv_full[st], Cfg::kStageBytes);
+          armed_mask |= 1u << st;
+          armed_parity = (armed_parity & ~(1u << st)) | (ph << st);
+          for (int pl = 0; pl < kPl; ++pl) {
+            tma_load_3d(sk + pl * Cfg::kKBytes, &kmap, &kv_full[st], (g.h * kPl + pl) * D, (g.jb0 + j) * kBlockN,
+                        g.b);
+            tma_load_3d(sk + (kPl + pl) * Cfg::kKBytes, &vmap, &kv_full[st], (g.h * kPl + pl) * D,
+                        (g.jb0 + j) * kBlockN, g.b);
+          }
         }
       }
       if (*abort_flag) {
+        // Let every armed TMA land before the CTA releases its shared memory
+        // (earlier Q loads were consumed before the last one was issued).
         volatile int never = 0;
-        mbar_wait(q_full, 0, &never, status);
+        if (qloads > 0) mbar_wait(q_full, (qloads - 1) & 1, &never, status);
         for (int s = 0; s < Cfg::kStages; ++s)
           if (armed_mask & (1u << s)) mbar_wait(&kv_full[s], (armed_parity >> s) & 1u, &never, status);
       }
@@ -216,15 +295,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kBlockM, kBlockN, BF16 ? 1u : 0u, 0u, 0u);
       constexpr uint32_t idesc_pv = make_idesc_f16(kBlockM, D, BF16 ? 1u : 0u, 0u, 1u);
-      bool ok = mbar_wait(q_full, 0, abort_flag, status);
-      for (int j = 0; ok && j <= nblocks; ++j) {
-        const int st = j % Cfg::kStages;
-        const int pst = (j + Cfg::kStages - 1) % Cfg::kStages;  // stage of block j - 1
-        if (j < nblocks && !mbar_wait(&kv_full[st], (j / Cfg::kStages) & 1, abort_flag, status)) break;
+      AttnSched sc = sched_begin(p);
+      AttnSeg g;
+      long long blk = 0;  // key blocks of earlier segments
+      int seg = 0;
+      bool ok = true;
+      while (ok && sched_next(p, sc, g)) {
+      ok = mbar_wait(q_full, seg & 1, abort_flag, status);
+      for (int j = 0; ok && j <= g.nblocks; ++j) {
+        const long long cur = blk + j;  // this block's position in the K/V ring and the tile barriers
+        const int st = static_cast<int>(cur % Cfg::kStages);
+        const int pst = static_cast<int>((cur + Cfg::kStages - 1) % Cfg::kStages);  // stage of block j - 1
+        if (j < g.nblocks &&
+            !mbar_wait(&kv_full[st], static_cast<uint32_t>(cur / Cfg::kStages) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
         for (int t = 0; t < 2 && ok; ++t) {
           if (j > 0) {
-            // P_t(j-1) is in shared memory (and S_t is free): O_t += P_t V_{j-1}.
-            if (!mbar_wait(&p_ready[t], (j - 1) & 1, abort_flag, status)) {
+            // P_t(j-1) is in TMEM over S_t: O_t += P_t V_{j-1}.
+            if (!mbar_wait(&p_ready[t], static_cast<uint32_t>(cur - 1) & 1u, abort_flag, status)) {
               ok = false;
               break;
             }
@@ -250,7 +340,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             umma_commit(&pv_done[t]);
             if (t == 1) umma_commit(&kv_empty[pst]);
           }
-          if (j < nblocks) {
+          if (j < g.nblocks) {
             // S_t(j) = Q_t K_j^T (split: Qh Kh + Qh Kl + Ql Kh)
             const uint32_t q_addr = smem_u32(smem + t * kPl * Cfg::kQBytes);
             const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * Cfg::kStageBytes);
@@ -270,6 +360,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
+      umma_commit(q_empty);  // arrives when the segment's S MMAs (readers of Q) are done
+      blk += g.nblocks;
+      ++seg;
+      }
       umma_commit(drain);
       volatile int never = 0;
       mbar_wait(drain, 0, &never, status);
@@ -286,16 +380,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tmem_s = tmem + t * 128 + lane_base;
     const uint32_t tmem_o = tmem + 256 + t * 128 + lane_base;
     const float c = p.scale_log2;
+    AttnSched sc = sched_begin(p);
+    AttnSeg g;
+    long long blk = 0;  // key blocks of earlier segments
+    int seg = 0;
+    bool ok = true;
+    while (ok && sched_next(p, sc, g)) {
     float m_ref = -INFINITY;  // reference maximum (raw scores) of the probabilities in O and l
     float l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nblocks; ++j) {
-      if (!warp_wait(&s_full[t], j & 1, abort_flag, status)) {
+    for (int j = 0; j < g.nblocks; ++j) {
+      const long long cur = blk + j;
+      if (!warp_wait(&s_full[t], static_cast<uint32_t>(cur) & 1u, abort_flag, status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int valid = min(kBlockN, p.lk - (jb0 + j) * kBlockN);
+      const int valid = min(kBlockN, p.lk - (g.jb0 + j) * kBlockN);
       uint32_t sr[kBlockN];
 #pragma unroll
       for (int c0 = 0; c0 < kBlockN; c0 += 32) {
@@ -326,7 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float alpha = first ? 0.f : exp2f((m_ref - m_new) * c);
       if (j > 0) {
         // PV_t(j-1) finished: the P buffer is free and O holds blocks < j.
-        if (!warp_wait(&pv_done[t], (j - 1) & 1, abort_flag, status)) {
+        if (!warp_wait(&pv_done[t], static_cast<uint32_t>(cur - 1) & 1u, abort_flag, status)) {
           ok = false;
           break;
         }
@@ -393,23 +493,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[t]);
     }
-    const bool done = ok && warp_wait(&pv_done[t], (nblocks - 1) & 1, abort_flag, status);
-    if (done && p.kv_splits > 1 && !SPLIT) {
-      // Partial over this CTA's keys: raw O row, reference max and sum.
+    const bool done = ok && warp_wait(&pv_done[t], static_cast<uint32_t>(blk + g.nblocks - 1) & 1u, abort_flag,
+                                      status);
+    if (!done) ok = false;
+    const int q0 = g.q0, h = g.h, b = g.b;
+    if (done && !g.whole) {
+      // Partial over this segment's keys: raw O row (hi + lo / 2048 for the
+      // split form), reference max and sum.
       tc_fence_after();
       const int qrow = q0 + t * kBlockM + row;
-      const long long prow = ((static_cast<long long>(split) * p.batch + b) * p.heads + h) * p.lq + qrow;
+      long long prow;
+      if (p.sk_ctas > 0)
+        prow = (static_cast<long long>(blockIdx.x) * p.sk_slots + seg) * (2 * kBlockM) + t * kBlockM + row;
+      else
+        prow = ((static_cast<long long>(blockIdx.x % p.kv_splits) * p.batch + b) * p.heads + h) * p.lq + qrow;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
-        uint32_t r[16];
+        uint32_t r[16], lo[16];
         tmem_ld16(tmem_o + c0, r);
+        if constexpr (SPLIT) tmem_ld16(tmem_o + D + c0, lo);
         tmem_wait_ld();
         if (qrow < p.lq) {
           float4* o4 = reinterpret_cast<float4*>(p.o_part + prow * D + c0);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            o4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
-                                __uint_as_float(r[4 * i + 3]));
+          for (int i = 0; i < 4; ++i) {
+            float4 o = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                   __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            if constexpr (SPLIT) {
+              o.x += __uint_as_float(lo[4 * i]) * (1.0f / 2048.0f);
+              o.y += __uint_as_float(lo[4 * i + 1]) * (1.0f / 2048.0f);
+              o.z += __uint_as_float(lo[4 * i + 2]) * (1.0f / 2048.0f);
+              o.w += __uint_as_float(lo[4 * i + 3]) * (1.0f / 2048.0f);
+            }
+            o4[i] = o;
+          }
         }
       }
       if (qrow < p.lq) *reinterpret_cast<float2*>(p.ml_part + prow * 2) = make_float2(m_ref, l);
@@ -465,7 +582,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
     }
+    // the O reads above come before this warpgroup's next p_ready arrive
     tc_fence_before();
+    blk += g.nblocks;
+    ++seg;
+    }
   }
   }
 
@@ -542,6 +663,103 @@ __global__ void attn_split_kernel(const float* src, int src_ld, long long rows, 
   *reinterpret_cast<uint4*>(o + d) = lo_raw;
 }
 
+// Merge the stream-K segments of the query rows of each pair that was split
+// over several CTAs (a pair one CTA held whole was written by that CTA): M =
+// max of the segments' reference maxima, out = sum_s w_s O_s / sum_s w_s l_s
+// with w_s = 2^((m_s - M) c), rounded once.  Block (pair, group of 8 rows):
+// thread 0 finds the covering CTAs (unit u belongs to CTA ((u + 1) G - 1) / U
+// of the even cut) and their slot rows; then one warp per query row, lane i
+// on dims i and i + 32, all segments' loads issued together.
+constexpr int kMergeMaxCtas = 8;
+constexpr int kMergeRows = 8;  // query rows per block (one per warp)
+
+template <int D, typename OutT>
+__global__ void attn_sk_merge_kernel(const AttnParams p, unsigned int* status) {
+  pdl_begin();
+  __shared__ long long slot_row[kMergeMaxCtas];
+  __shared__ int ncta;
+  constexpr int kGroups = 2 * kBlockM / kMergeRows;
+  const long long pair = blockIdx.x / kGroups;
+  if (threadIdx.x == 0) {
+    const long long u_first = pair * p.sk_nb, u_last = u_first + p.sk_nb - 1;
+    const long long c0 = ((u_first + 1) * p.sk_ctas - 1) / p.sk_units;
+    const long long c1 = ((u_last + 1) * p.sk_ctas - 1) / p.sk_units;
+    int n = 0;
+    if (c1 - c0 + 1 > kMergeMaxCtas) {
+      n = -1;  // the plan never cuts a pair this finely (at least 8 blocks per CTA)
+    } else if (c0 != c1) {
+      for (long long cta = c0; cta <= c1; ++cta, ++n)
+        slot_row[n] = (cta * p.sk_slots + (pair - sk_unit0(p, cta) / p.sk_nb)) * (2 * kBlockM);
+    }
+    ncta = n;
+  }
+  __syncthreads();
+  const int n = ncta;
+  const long long bh = pair / p.sk_pairs;
+  const int r = static_cast<int>(blockIdx.x % kGroups) * kMergeRows + (threadIdx.x >> 5);
+  const int q = static_cast<int>(pair - bh * p.sk_pairs) * 2 * kBlockM + r;
+  if (n > 0 && q < p.lq) {
+    const int lane = threadIdx.x & 31;
+    const int h = static_cast<int>(bh % p.heads);
+    const int b = static_cast<int>(bh / p.heads);
+    float2 ml[kMergeMaxCtas];
+    float o0[kMergeMaxCtas], o1[kMergeMaxCtas];
+#pragma unroll
+    for (int k = 0; k < kMergeMaxCtas; ++k) {
+      if (k < n) {
+        const long long srow = slot_row[k] + r;
+        ml[k] = *reinterpret_cast<const float2*>(p.ml_part + srow * 2);
+        const float* o = p.o_part + srow * D;
+        o0[k] = lane < D ? o[lane] : 0.f;
+        o1[k] = lane + 32 < D ? o[lane + 32] : 0.f;
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kMergeMaxCtas; ++k)
+      if (k < n) mx = fmaxf(mx, ml[k].x);
+    float den = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMergeMaxCtas; ++k) {
+      if (k < n) {
+        const float wgt = exp2f((ml[k].x - mx) * p.scale_log2);
+        den = fmaf(wgt, ml[k].y, den);
+        a0 = fmaf(wgt, o0[k], a0);
+        a1 = fmaf(wgt, o1[k], a1);
+      }
+    }
+    const float inv = 1.f / den;
+    OutT* out = static_cast<OutT*>(p.out) + (static_cast<long long>(b) * p.lq + q) * p.out_ld + h * D;
+    if (lane < D) out[lane] = static_cast<OutT>(a0 * inv);
+    if (lane + 32 < D) out[lane + 32] = static_cast<OutT>(a1 * inv);
+  } else if (n < 0 && threadIdx.x == 0) {
+    set_bad_shape(status);
+  }
+  if (p.clock && threadIdx.x == 0) atomicMax(p.clock + 1, static_cast<unsigned long long>(globaltimer_ns()));
+}
+
+// Stream-K plan for a grid of `ctas` CTAs (query pairs x heads x batch) over
+// `blocks` key blocks each, when the grid leaves a large share of the SMs
+// idle in its last wave (and small grids are not already split over keys):
+// every SM takes an equal range of (pair, key block) units, at least 8
+// blocks.  Returns the CTAs (0: plain schedule) and the partial slots per CTA.
+int choose_stream_k(long long ctas, int blocks, int* slots) {
+  const int sms = sm_count();
+  *slots = 0;
+  static const bool enabled = [] {
+    const char* v = std::getenv("LDB_ATTN_STREAMK");
+    return !(v && v[0] == '0');
+  }();
+  if (!enabled || ctas * 2 <= sms || blocks < 8) return 0;
+  const long long waves = (ctas + sms - 1) / sms;
+  if (ctas * 10 >= waves * sms * 9) return 0;  // the plain grid already fills 90 % of the waves
+  const long long units = ctas * blocks;
+  const long long per = (units + sms - 1) / sms;
+  if (per < 8) return 0;
+  *slots = static_cast<int>((per + blocks - 1) / blocks) + 1;
+  return sms;
+}
+
 // Key splits for a grid of `ctas` CTAs over `blocks` key blocks.  Splitting
 // costs a partial write, a merge launch and per-CTA set-up, which only pays
 // when the unsplit grid leaves most SMs idle (measured: 32 CTAs of 800
@@ -579,9 +797,18 @@ int launch_attn(cudaStream_t stream, const CUtensorMap& qm, const CUtensorMap& k
     return fail(LDB_ERR_CUDA, "attention kernel launches with %d registers per thread; the register split needs %d",
                 launch_regs, kAttnLaunchRegs);
   dim3 grid(((p.lq + 2 * kBlockM - 1) / (2 * kBlockM)) * p.kv_splits, p.heads, p.batch);
+  if (p.sk_ctas > 0) grid = dim3(p.sk_ctas, 1, 1);
   int r = launch_kernel(kernel, grid, dim3(kAttnThreads), Cfg::kSmemBytes, stream, "attention launch", qm, km, vm,
                         p, device_status_ptr());
-  if (r != LDB_OK || p.kv_splits == 1) return r;
+  if (r != LDB_OK) return r;
+  if (p.sk_ctas > 0) {
+    using OutT = typename std::conditional<SPLIT, float,
+                                           typename std::conditional<BF16, __nv_bfloat16, __half>::type>::type;
+    const long long blocks = p.sk_units / p.sk_nb * (2 * kBlockM / kMergeRows);
+    return launch_kernel(attn_sk_merge_kernel<D, OutT>, dim3(static_cast<unsigned>(blocks)), dim3(32 * kMergeRows),
+                         0, stream, "attention merge launch", p, device_status_ptr());
+  }
+  if (p.kv_splits == 1) return r;
   const long long rows = static_cast<long long>(p.batch) * p.heads * p.lq;
   return launch_kernel(attn_combine_kernel<D, BF16>, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
                        stream, "attention combine launch", p);
@@ -639,15 +866,29 @@ static int flash_attention_impl(cudaStream_t stream, const void* q, int q_ld, co
   p.kv_splits = 1;
   p.blocks_per_split = blocks;
   p.o_part = p.ml_part = nullptr;
+  p.sk_ctas = 0;
+  p.sk_nb = blocks;
+  p.sk_pairs = (lq + 2 * kBlockM - 1) / (2 * kBlockM);
+  p.sk_slots = 0;
+  p.sk_units = 0;
   if (workspace) {
     const int splits = choose_kv_splits(ctas, blocks);
     const size_t rows = static_cast<size_t>(batch) * heads * lq;
     const size_t need = static_cast<size_t>(splits) * rows * (head_dim + 2) * sizeof(float);
+    int slots = 0;
+    const int sk = choose_stream_k(ctas, blocks, &slots);
+    const size_t sk_rows = static_cast<size_t>(sk) * slots * 2 * kBlockM;
     if (splits > 1 && workspace_bytes >= need) {
       p.kv_splits = splits;
       p.blocks_per_split = (blocks + splits - 1) / splits;
       p.o_part = static_cast<float*>(workspace);
       p.ml_part = p.o_part + static_cast<size_t>(splits) * rows * head_dim;
+    } else if (sk > 0 && workspace_bytes >= sk_rows * (head_dim + 2) * sizeof(float)) {
+      p.sk_ctas = sk;
+      p.sk_slots = slots;
+      p.sk_units = ctas * blocks;
+      p.o_part = static_cast<float*>(workspace);
+      p.ml_part = p.o_part + sk_rows * head_dim;
     }
   }
   if (head_dim == 64) return bf16 ? launch_attn<64, true>(stream, qm, km, vm, p) : launch_attn<64, false>(stream, qm, km, vm, p);
@@ -670,7 +911,12 @@ int ldb_flash_attention_workspace_size(int batch, int lq, int lk, int heads, int
   const int blocks = (lk + kBlockN - 1) / kBlockN;
   const long long ctas = static_cast<long long>((lq + 2 * kBlockM - 1) / (2 * kBlockM)) * heads * batch;
   const int splits = choose_kv_splits(ctas, blocks);
-  *bytes = splits > 1 ? static_cast<size_t>(splits) * batch * heads * lq * (head_dim + 2) * sizeof(float) : 0;
+  int slots = 0;
+  const int sk = choose_stream_k(ctas, blocks, &slots);
+  const size_t split_bytes =
+      splits > 1 ? static_cast<size_t>(splits) * batch * heads * lq * (head_dim + 2) * sizeof(float) : 0;
+  const size_t sk_bytes = static_cast<size_t>(sk) * slots * 2 * kBlockM * (head_dim + 2) * sizeof(float);
+  *bytes = std::max(split_bytes, sk_bytes);
   return LDB_OK;
 }
 
@@ -693,8 +939,15 @@ int ldb_flash_attention_f32_workspace_size(int batch, int lq, int lk, int heads,
   if (!bytes) return fail(LDB_ERR_INVALID, "bytes is null");
   if (batch <= 0 || lq <= 0 || lk <= 0 || heads <= 0 || head_dim <= 0)
     return fail(LDB_ERR_SHAPE, "extents must be positive");
-  // split planes of Q, K and V: (rows, heads * 2 * head_dim) f16 each
-  *bytes = static_cast<size_t>(batch) * (static_cast<size_t>(lq) + 2 * lk) * heads * head_dim * 2 * 2;
+  // split planes of Q, K and V: (rows, heads * 2 * head_dim) f16 each, then
+  // the stream-K partial rows (256-byte aligned)
+  const size_t planes = static_cast<size_t>(batch) * (static_cast<size_t>(lq) + 2 * lk) * heads * head_dim * 2 * 2;
+  const int blocks = (lk + kBlockN - 1) / kBlockN;
+  const long long ctas = static_cast<long long>((lq + 2 * kBlockM - 1) / (2 * kBlockM)) * heads * batch;
+  int slots = 0;
+  const int sk = choose_stream_k(ctas, blocks, &slots);
+  *bytes = (planes + 255) / 256 * 256 +
+           static_cast<size_t>(sk) * slots * 2 * kBlockM * (head_dim + 2) * sizeof(float);
   return LDB_OK;
 }
 
@@ -766,6 +1019,20 @@ int ldb_flash_attention_f32(cudaStream_t stream, const float* q, int q_ld, const
   p.blocks_per_split = (lk + kBlockN - 1) / kBlockN;
   p.o_part = p.ml_part = nullptr;
   p.clock = nullptr;
+  p.sk_nb = p.blocks_per_split;
+  p.sk_pairs = (lq + 2 * kBlockM - 1) / (2 * kBlockM);
+  {
+    const long long ctas = static_cast<long long>(p.sk_pairs) * heads * batch;
+    int slots = 0;
+    p.sk_ctas = choose_stream_k(ctas, p.sk_nb, &slots);
+    p.sk_slots = slots;
+    p.sk_units = ctas * p.sk_nb;
+    if (p.sk_ctas > 0) {
+      const size_t planes = static_cast<size_t>(batch) * (static_cast<size_t>(lq) + 2 * lk) * width * 2;
+      p.o_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (planes + 255) / 256 * 256);
+      p.ml_part = p.o_part + static_cast<size_t>(p.sk_ctas) * slots * 2 * kBlockM * head_dim;
+    }
+  }
   if (head_dim == 64) return launch_attn<64, false, true>(stream, qm, km, vm, p);
   if (head_dim == 16) return launch_attn<16, false, true>(stream, qm, km, vm, p);
   return launch_attn<32, false, true>(stream, qm, km, vm, p);

@@ -107,7 +107,8 @@ def test_layer_norm(cuda_device):
         (2, 300, 200, 2, 2.0, 32),  # partial query and key tiles
         (1, 640, 77, 2, 2.0, 32),  # cross-attention, one partial key block
         (1, 2048, 2048, 4, 6.0, 32),  # peaked softmax: the running maximum moves
-        (1, 23104, 23104, 2, 1.0, 32),  # LMNet's 16 x 38 x 38 level, 2 heads of 32
+        (1, 23104, 23104, 2, 1.0, 32),  # LMNet's 16 x 38 x 38 level, 2 heads of 32 (stream-K)
+        (1, 4000, 1000, 16, 2.0, 32),  # stream-K with up to 3 segments per CTA, partial tiles
     ],
 )
 def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale, d):
@@ -147,6 +148,8 @@ def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale, d):
         (2, 300, 200, 4, 64, torch.bfloat16, False),
         (1, 6400, 6400, 8, 64, torch.bfloat16, False),  # config-2 self-attention
         (1, 6400, 77, 8, 64, torch.bfloat16, False),  # config-2 cross-attention
+        (1, 6400, 6400, 4, 64, torch.float16, False),  # stream-K: 100 pairs on all SMs, 2 segments per CTA
+        (1, 4000, 1000, 16, 64, torch.float16, False),  # stream-K, up to 3 segments per CTA, partial tiles
     ],
 )
 def test_flash_attention(cuda_device, batch, lq, lk, heads, d, dtype, ties):
