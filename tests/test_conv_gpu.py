@@ -260,6 +260,38 @@ def test_conv_fp32_exact_mode(cuda_device, shape, out_channels, stride):
     assert rel_l2(actual, expected) <= 1e-4
 
 
+@pytest.mark.parametrize("shape,cout", [((1, 128, 8, 10, 12), 128), ((1, 512, 4, 5, 6), 512)])
+def test_device_clock_records_each_launch(cuda_device, shape, cout):
+    """The device-clock timing of a conv launch (plain, and split-K with its
+    reduce) and of an attention launch: end after start, within the event
+    time of the launch, results unchanged."""
+    from lesiondiffusion_mlx_b200 import instrument, ops
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_weight
+
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    x = torch.randn((shape[0], *shape[2:], shape[1]), generator=g, device=cuda_device).half()
+    w = (torch.randn((cout, shape[1], 3, 3, 3), generator=g, device=cuda_device) * 0.02).half()
+    packed = pack_weight(w)
+    q = torch.randn((1, 700, 128), generator=g, device=cuda_device).half()
+    want = conv3d_ndhwc(x, packed)
+    want_attn = ops.flash_attention(q, q, q, heads=2, scale=0.125)
+    timer = instrument.KernelTimer(device_clock=True)
+    timer.arm(x.device)
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    with instrument.timing(timer):
+        got = conv3d_ndhwc(x, packed)
+        got_attn = ops.flash_attention(q, q, q, heads=2, scale=0.125)
+    e.record()
+    torch.cuda.synchronize()
+    summary = timer.summary()
+    assert torch.equal(got, want) and torch.equal(got_attn, want_attn)
+    for kind in ("conv3d", "attention"):
+        assert summary[kind]["launches"] == 1
+        assert 0 < summary[kind]["ms"] <= s.elapsed_time(e)
+
+
 def test_device_status_clean(cuda_device):
     from lesiondiffusion_mlx_b200 import _lib
 
