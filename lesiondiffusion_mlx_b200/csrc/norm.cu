@@ -265,8 +265,12 @@ __device__ __forceinline__ void prepare_store(const float (&v)[8], int c, int c_
   if (split) *reinterpret_cast<uint4*>(o + cpad) = lo_raw;
 }
 
-// Voxels [0, voxels) of the batch item starting at global voxel v0.
-__device__ __forceinline__ void prepare_pass(const Src2& s, long long v0, int voxels, const Affine8& a, int c,
+// Voxels [0, voxels) of the batch item starting at global voxel v0.  The
+// thread's first four loads go out before `get_affine()` is called (they only
+// need the input), so deriving the affine overlaps their latency; every
+// thread of the block calls get_affine() exactly once.
+template <class GetAffine>
+__device__ __forceinline__ void prepare_pass(const Src2& s, long long v0, int voxels, GetAffine get_affine, int c,
                                              int silu, int split, int cpad, __half* out, int out_ld) {
   const int c_total = s.c1 + s.c2;
   const int vecs = cpad / 8;
@@ -274,6 +278,25 @@ __device__ __forceinline__ void prepare_pass(const Src2& s, long long v0, int vo
   const long long stride = static_cast<long long>(gridDim.x) * rows;
   const bool live = c + 8 <= c_total;
   long long v = static_cast<long long>(blockIdx.x) * rows + threadIdx.x / vecs;
+  Affine8 a;
+  {
+    float x[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (live && v + u * stride < voxels) {
+        load8(s, v0 + v + u * stride, c, x[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[u][j] = 0.f;
+      }
+    }
+    a = get_affine();
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v + u * stride < voxels)
+        prepare_store(x[u], c, c_total, a, silu, split, cpad, out + (v0 + v + u * stride) * out_ld + c);
+    v += 4 * stride;
+  }
   for (; v + 3 * stride < voxels; v += 4 * stride) {
     float x[4][8];
 #pragma unroll
@@ -308,9 +331,11 @@ __global__ void prepare_kernel(Src2 s, int voxels_per_batch, const float* affine
   const int c_total = s.c1 + s.c2;
   const int c = (threadIdx.x % (cpad / 8)) * 8;
   const int b = blockIdx.y;
-  const Affine8 a = load_affine8(affine ? affine + (static_cast<long long>(b) * c_total + c) * 2 : nullptr, c, c_total);
-  prepare_pass(s, static_cast<long long>(b) * voxels_per_batch, voxels_per_batch, a, c, silu, split, cpad, out,
-               out_ld);
+  auto get_affine = [&] {
+    return load_affine8(affine ? affine + (static_cast<long long>(b) * c_total + c) * 2 : nullptr, c, c_total);
+  };
+  prepare_pass(s, static_cast<long long>(b) * voxels_per_batch, voxels_per_batch, get_affine, c, silu, split, cpad,
+               out, out_ld);
 }
 
 // GroupNorm affine of batch item b from producer statistics (per channel FP64
@@ -404,10 +429,12 @@ __global__ void prepare_stats_kernel(Src2 s, int voxels, int stat_voxels, const 
   const int b = blockIdx.y;
   stage_gamma_beta(gamma, beta, C, aff);
   pdl_begin();
-  block_affine_from_stats(st1, s.c1, st2, s.c2, b, groups, stat_voxels, eps, aff, sts, gm);
   const int c = (threadIdx.x % (cpad / 8)) * 8;
-  const Affine8 a = load_affine8(c < C ? aff + c * 2 : nullptr, c, C);
-  prepare_pass(s, static_cast<long long>(b) * voxels, voxels, a, c, silu, split, cpad, out, out_ld);
+  auto get_affine = [&] {
+    block_affine_from_stats(st1, s.c1, st2, s.c2, b, groups, stat_voxels, eps, aff, sts, gm);
+    return load_affine8(c < C ? aff + c * 2 : nullptr, c, C);
+  };
+  prepare_pass(s, static_cast<long long>(b) * voxels, voxels, get_affine, c, silu, split, cpad, out, out_ld);
 }
 
 // LayerNorm over the last axis of (rows, C) f16 (mlx_model.py:360-367):
