@@ -1130,7 +1130,8 @@ bool conv_trans_enabled() {
 // Tile-selection overrides for measurements (read on every plan): LDB_CONV_BN
 // (64 or 128) replaces the 256-column tile where the packed weight rows are
 // the same (out_channels a multiple of 256); LDB_CONV_SPLITS fixes the
-// split-K factor.  Unset or 0: the planner's choice.
+// split-K factor; LDB_CONV_TRANS_BD (1..4) the brick depth of the
+// channel-major tile.  Unset or 0: the planner's choice.
 int env_int(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::atoi(v) : 0;
@@ -1268,7 +1269,9 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     const long long th = (gh + 7) / 8, tw = (gw + 7) / 8;
     int best_bd = 1;
     long long best_cost = -1;
+    const int force_bd = env_int("LDB_CONV_TRANS_BD");  // tuning override, 1..4
     for (int cand = 1; cand <= 4; ++cand) {
+      if (force_bd >= 1 && force_bd <= 4 && cand != force_bd) continue;
       const long long tiles = static_cast<long long>(B) * ((gd + cand - 1) / cand) * th * tw * p.parities;
       const long long cost = ((tiles + sms - 1) / sms) * (64LL * cand + 64);
       if (best_cost < 0 || cost <= best_cost) {
