@@ -616,7 +616,11 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
       rbuf = res_base + rb * Cfg::kEpiBufBytes;
     }
     const bool dvalid = d0 + pl < p.grid_d;
-    float s1 = 0.f, s2 = 0.f;
+    // Each step is its own straight loop with the optional parts (residual,
+    // GELU, statistics) branched around as a whole: a per-value branch over
+    // an inlined GELU spreads the 64 executed iterations over tens of KB of
+    // code, and the instruction fetch, not the arithmetic, then sets the
+    // per-plane time.
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = (v[j] + add) * p.out_scale;
     if (rbuf) {  // all residual reads before the first staging store (see epilogue_tile)
@@ -625,23 +629,29 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
         v[j] += __half2float(*reinterpret_cast<const __half*>(
             rbuf + box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128)));
     }
+    if (p.act == kActGelu) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const uint32_t off = box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128);
-      float y = v[j];
-      if (p.act == kActGelu) y = gelu_erf_f32(__half2float(__float2half_rn(y)));
-      const __half h = __float2half_rn(y);
-      if (live) *reinterpret_cast<__half*>(ob + off) = h;
-      if (dvalid && ((plane_mask >> j) & 1ull)) {
-        const float d = __half2float(h) - st.run_k;
-        s1 += d;
-        s2 = fmaf(d, d, s2);
-      }
+      for (int j = 0; j < 64; ++j) v[j] = gelu_erf_f32(__half2float(__float2half_rn(v[j])));
     }
-    if (p.stats && dvalid) {
-      st.run_s1 += s1;
-      st.run_s2 += s2;
-      st.run_rows += __popcll(plane_mask);
+    if (live) {  // round once; the statistics below read the rounded values
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const __half h = __float2half_rn(v[j]);
+        v[j] = __half2float(h);
+        *reinterpret_cast<__half*>(ob + box_off + swizzle_offset(static_cast<uint32_t>(j) * 128 + col_off, 128)) = h;
+      }
+      if (p.stats && dvalid) {
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float d = ((plane_mask >> j) & 1ull) ? v[j] - st.run_k : 0.f;
+          s1 += d;
+          s2 = fmaf(d, d, s2);
+        }
+        st.run_s1 += s1;
+        st.run_s2 += s2;
+        st.run_rows += __popcll(plane_mask);
+      }
     }
     fence_proxy_async_smem();
     named_barrier(1, 128);
@@ -1262,8 +1272,10 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   // brick), the efficient 128 x 256 shape at bd = 4 where a 128-channel
   // voxel-major tile would run 128 x 128.  bd minimises waves x tile size.
   // (64-channel K blocks only: with 16 / 32 input channels per block the
-  // per-block overhead dominates and the voxel-major tile is faster.)
-  const bool trans_ok = !exact && p.k_splits == 1 && kc == 64 &&
+  // per-block overhead dominates and the voxel-major tile is faster.  3x3x3
+  // kernels only: a pointwise conv has too few K blocks per tile to hide the
+  // per-plane transposed epilogue, and its voxel-major tile runs ~3x faster.)
+  const bool trans_ok = !exact && taps > 1 && p.k_splits == 1 && kc == 64 &&
                         (cout == 128 || (cout == 64 && p.parities == 1)) && conv_trans_enabled();
   if (trans_ok) {
     const long long th = (gh + 7) / 8, tw = (gw + 7) / 8;

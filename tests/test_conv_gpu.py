@@ -152,7 +152,7 @@ def test_pointwise_conv_and_gelu(cuda_device, shape, out_channels):
         ((1, 64, 45, 21, 27), 128, "conv", True),  # ragged planes and depth; shift + residual + scale
         ((1, 96, 41, 24, 24), 64, "conv", True),  # 64 output channels (weight rows past 64 read as zero)
         ((1, 32, 12, 16, 16), 128, "up", False),  # folded upsampling, 8 output parities
-        ((1, 256, 30, 24, 40), 128, "pw", False),  # pointwise, two 64-channel K blocks
+        ((1, 256, 30, 24, 40), 128, "pw", False),  # pointwise: planned voxel-major (the path it runs on)
     ],
 )
 def test_channel_major_tile(cuda_device, shape, out_channels, kind, extra):
