@@ -193,6 +193,24 @@ def test_channel_major_tile(cuda_device, shape, out_channels, kind, extra):
     assert np.all(error <= bound), f"max excess {(error - bound).max()}"
 
 
+def test_channel_major_tile_gelu(cuda_device):
+    """GELU in the channel-major epilogue: the conv output rounded to f16,
+    then the FP32 erf GELU, rounded once more (as the voxel-major tile)."""
+    from lesiondiffusion_mlx_b200 import _lib
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_weight
+
+    x, w, b = f16_case((1, 64, 19, 21, 17), 128, 3, seed=77)
+    xd = to_ndhwc(x.to(cuda_device))
+    packed = pack_weight(w.to(cuda_device))
+    plain = conv3d_ndhwc(xd, packed, b.to(cuda_device).float())
+    gelu = conv3d_ndhwc(xd, packed, b.to(cuda_device).float(), act=_lib.LDB_ACT_GELU)
+    torch.cuda.synchronize()
+    rounded = plain.permute(0, 4, 1, 2, 3).double().cpu()
+    expected = (rounded * 0.5 * (1 + torch.erf(rounded / np.sqrt(2)))).numpy()
+    actual = gelu.permute(0, 4, 1, 2, 3).double().cpu().numpy()
+    assert np.all(np.abs(actual - expected) <= 2 * half_spacing(expected) + 1e-6)
+
+
 @pytest.mark.parametrize("shape,out_channels", [((1, 16, 8, 8, 8), 16), ((2, 32, 7, 9, 6), 48),
                                                 ((1, 64, 24, 20, 30), 64)])
 def test_stride2_conv_padded_after_only(cuda_device, shape, out_channels):
