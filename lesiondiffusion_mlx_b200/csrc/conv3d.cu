@@ -744,6 +744,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_parity = 0;
       bool waited = false;
+      uint8_t* stage_ptr = smem;  // smem + stage * kStageBytes
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord c = decode_tile(p, t);
         const int kb0 = c.ks * p.kb_per_split;
@@ -752,63 +753,94 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int pd = c.par >> 2, ph = (c.par >> 1) & 1, pw = c.par & 1;
         const int brow = c.par * p.wrows_per_parity + c.nt * BN;
         bool ok = true;
+        // Tap digits (kd, kh, kw; for the folded up-conv the bits td, th, tw)
+        // and input-channel chunk of kb0, then advanced by counters: the one
+        // producer thread's instruction path per K block sets the pipeline's
+        // rate when K blocks are small, so it holds no division.  The weight
+        // column of K block kb is kb * KC (tap * cin_pad + chunk * KC).
+        int tap = kb0 / p.cin_chunks;
+        int chunk = kb0 - tap * p.cin_chunks;
+        int kd, kh, kw;
+        if (p.mode == kConvUp2) {
+          kd = tap >> 2;
+          kh = (tap >> 1) & 1;
+          kw = tap & 1;
+        } else {
+          kd = tap / 9;
+          kh = (tap / 3) % 3;
+          kw = tap % 3;
+        }
+        const int zb = d0 + p.in_zoff;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * Cfg::kStageBytes;
+          uint8_t* sa = stage_ptr;
           uint8_t* sb = sa + Cfg::kPlanes * Cfg::kABytes;
           mbar_arrive_expect_tx(&full[stage], tx_bytes);
           armed_mask |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          const int tap = kb / p.cin_chunks;
-          const int chn = (kb - tap * p.cin_chunks) * KC;
-          int map = 0, x = w0, y = h0, z = d0;
+          int map = 0, x = w0, y = h0, z = zb;
           if (p.mode == kConv3x3x3) {
-            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
-            x = w0 + kw - 1;
-            y = h0 + kh - 1;
-            z = d0 + kd - 1;
+            x += kw - 1;
+            y += kh - 1;
+            z += kd - 1;
           } else if (p.mode == kConv3x3x3S2) {
             // input index 2o + k - 1: k = 1 -> parity 0 at o; k = 0 -> parity 1
             // at o - 1; k = 2 -> parity 1 at o.
-            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
             map = (kd != 1) * 4 + (kh != 1) * 2 + (kw != 1);
-            x = w0 - (kw == 0);
-            y = h0 - (kh == 0);
-            z = d0 - (kd == 0);
+            x -= (kw == 0);
+            y -= (kh == 0);
+            z -= (kd == 0);
           } else if (p.mode == kConv3x3x3S2Pad01) {
             // input index 2o + k (no padding before): k = 0 -> parity 0 at o,
             // k = 1 -> parity 1 at o, k = 2 -> parity 0 at o + 1 (past the end:
             // the zero padding after).
-            const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
             map = (kd == 1) * 4 + (kh == 1) * 2 + (kw == 1);
-            x = w0 + (kw == 2);
-            y = h0 + (kh == 2);
-            z = d0 + (kd == 2);
+            x += (kw == 2);
+            y += (kh == 2);
+            z += (kd == 2);
           } else if (p.mode == kConvUp2) {
             // parity p, folded tap t reads source index m + p + t - 1.
-            const int td = tap >> 2, th = (tap >> 1) & 1, tw = tap & 1;
-            x = w0 + pw + tw - 1;
-            y = h0 + ph + th - 1;
-            z = d0 + pd + td - 1;
+            x += pw + kw - 1;
+            y += ph + kh - 1;
+            z += pd + kd - 1;
           }
-          z += p.in_zoff;
           if (!waited) {
             pdl_wait();
             waited = true;
             if (p.clock) atomicMin(p.clock, static_cast<unsigned long long>(globaltimer_ns()));
           }
+          const int chn = chunk * KC;
           tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
-          tma_load_2d(sb, &wmap, &full[stage], tap * p.cin_pad + chn, brow);
+          tma_load_2d(sb, &wmap, &full[stage], kb * KC, brow);
           if (EXACT) {
             tma_load_5d(sa + Cfg::kABytes, &maps.a[map], &full[stage], p.cin_pad + chn, x, y, z, c.b);
-            tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + tap * p.cin_pad + chn, brow);
+            tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + kb * KC, brow);
+          }
+          if (++chunk == p.cin_chunks) {
+            chunk = 0;
+            if (p.mode == kConvUp2) {
+              kw ^= 1;
+              if (kw == 0) {
+                kh ^= 1;
+                if (kh == 0) ++kd;
+              }
+            } else if (++kw == 3) {
+              kw = 0;
+              if (++kh == 3) {
+                kh = 0;
+                ++kd;
+              }
+            }
           }
           if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
+            stage_ptr = smem;
+          } else {
+            stage_ptr += Cfg::kStageBytes;
           }
         }
         if (!ok) break;
@@ -826,6 +858,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
+      const uint32_t smem_base = smem_u32(smem);
+      uint32_t stage_addr = smem_base;  // shared address of the current stage
+      const uint64_t desc_const = make_smem_desc(0, 16, Cfg::kSbo, Cfg::kLayout);
+      const uint32_t trans_idesc = TRANS ? make_idesc_f16(128, p.trans_n, 0, 0, 0) : 0u;
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++local) {
         const TileCoord c = decode_tile(p, t);
         const int kb0 = c.ks * p.kb_per_split;
@@ -842,19 +878,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * Cfg::kStageBytes);
-          const uint32_t b_addr = a_addr + Cfg::kPlanes * Cfg::kABytes;
+          // Descriptors of the stage's tiles; the K = 16 step k starts 32
+          // bytes further, i.e. 2 in the 16-byte address field (which cannot
+          // carry: shared addresses are below 256 KB).
+          const uint64_t ad0 = desc_const | static_cast<uint64_t>((stage_addr >> 4) & 0x3FFFu);
+          const uint64_t bd0 = desc_const | static_cast<uint64_t>(((stage_addr + Cfg::kPlanes * Cfg::kABytes) >> 4) & 0x3FFFu);
 #pragma unroll
           for (int k = 0; k < KC / 16; ++k) {
-            const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-            const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+            const uint64_t ad = ad0 + 2 * k;
+            const uint64_t bd = bd0 + 2 * k;
             const int step = (kb - kb0) * (KC / 16) + k;  // K step within the tile
             const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
             if constexpr (TRANS) {
               // out^T: the weight tile is the M = 128 operand, the voxels are N
               const int chains = p.trans_chains;
-              umma_ss(d_hi + (chains == 2 ? (step & 1) * 128 : 0), bd, ad, make_idesc_f16(128, p.trans_n, 0, 0, 0),
-                      step >= chains ? 1u : 0u);
+              umma_ss(d_hi + (chains == 2 ? (step & 1) * 128 : 0), bd, ad, trans_idesc, step >= chains ? 1u : 0u);
               continue;
             }
             if constexpr (Cfg::kChains == 2) {
@@ -863,8 +901,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
             umma_ss(d_hi, ad, bd, Cfg::kIdesc, accum);
             if (EXACT) {
-              const uint64_t ad_lo = make_smem_desc(a_addr + Cfg::kABytes + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
-              const uint64_t bd_lo = make_smem_desc(b_addr + Cfg::kBBytes + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+              const uint64_t ad_lo = ad + (Cfg::kABytes >> 4);
+              const uint64_t bd_lo = bd + (Cfg::kBBytes >> 4);
               umma_ss(d_lo, ad, bd_lo, Cfg::kIdesc, accum);
               umma_ss(d_lo, ad_lo, bd, Cfg::kIdesc, 1u);
             }
@@ -873,6 +911,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
+            stage_addr = smem_base;
+          } else {
+            stage_addr += Cfg::kStageBytes;
           }
         }
         if (!ok) break;
