@@ -2,8 +2,9 @@
 //
 // GEMM view: rows M are output voxels (source voxels for the folded 2x
 // upsampling conv), columns N are output channels, and K runs over
-// (tap, input-channel block).  Nothing is im2col'ed: for each K block the
-// producer warp issues one 5-D TMA load of a bd x bh x bw brick of voxels x
+// (tap, input-channel block).  Nothing is im2col'ed: for each K block a
+// producer warp (two take alternate K blocks) issues one 5-D TMA load of a
+// bd x bh x bw brick of voxels x
 // KC channels of the NDHWC activation, offset by the tap; TMA's out-of-bounds
 // zero fill supplies the padding.  Weights are packed K-major
 // [parity][Cout][tap][Cin] and loaded as 2-D TMA tiles.  A single thread of
@@ -38,7 +39,8 @@ namespace ldb {
 
 namespace {
 
-constexpr int kConvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kConvWarps = 7;  // warps 0 and 6 TMA producers, warp 1 MMA, warps 2-5 epilogue
+constexpr int kConvThreads = 32 * kConvWarps;
 constexpr int kTileM = 128;
 
 struct TileCoord {
@@ -737,14 +739,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t a_box_bytes = static_cast<uint32_t>(KC * 2 * p.bw * p.bh * p.bd);
   const uint32_t tx_bytes = Cfg::kPlanes * (a_box_bytes + static_cast<uint32_t>(Cfg::kBBytesRaw));
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == kConvWarps - 1) {
+    // ------------------------------------------------------------ producers
+    // Two producer warps (0 and the last) take alternate K blocks of the
+    // CTA's sequence (flattened over its tiles): K block j goes to producer
+    // j % 2 and to stage j % kStages.  Per K block one thread waits for the
+    // stage, arms it and issues the loads, a path of some hundred cycles of
+    // dependent latency that sets the pipeline's rate when it runs on one
+    // thread; two run it side by side.
     if (lane == 0) {
-      int stage = 0;
+      const int pid = warp == 0 ? 0 : 1;
+      int stage = pid;
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_parity = 0;
       bool waited = false;
-      uint8_t* stage_ptr = smem;  // smem + stage * kStageBytes
+      int jt = 0;  // sequence index of the current tile's first K block
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord c = decode_tile(p, t);
         const int kb0 = c.ks * p.kb_per_split;
@@ -752,31 +761,35 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
         const int pd = c.par >> 2, ph = (c.par >> 1) & 1, pw = c.par & 1;
         const int brow = c.par * p.wrows_per_parity + c.nt * BN;
+        int kb = kb0 + ((jt + pid) & 1);  // this producer's first K block of the tile
+        jt += kb1 - kb0;
+        if (kb >= kb1) continue;
         bool ok = true;
         // Tap digits (kd, kh, kw; for the folded up-conv the bits td, th, tw)
-        // and input-channel chunk of kb0, then advanced by counters: the one
-        // producer thread's instruction path per K block sets the pipeline's
-        // rate when K blocks are small, so it holds no division.  The weight
-        // column of K block kb is kb * KC (tap * cin_pad + chunk * KC).
-        int tap = kb0 / p.cin_chunks;
-        int chunk = kb0 - tap * p.cin_chunks;
-        int kd, kh, kw;
-        if (p.mode == kConvUp2) {
-          kd = tap >> 2;
-          kh = (tap >> 1) & 1;
-          kw = tap & 1;
-        } else {
-          kd = tap / 9;
-          kh = (tap / 3) % 3;
-          kw = tap % 3;
+        // and channel chunk of kb, then advanced two K blocks at a time by
+        // counters (no division per K block).  The weight column of K block kb
+        // is kb * KC (tap * cin_pad + chunk * KC).
+        int chunk, kd, kh, kw;
+        {
+          const int tap = kb / p.cin_chunks;
+          chunk = kb - tap * p.cin_chunks;
+          if (p.mode == kConvUp2) {
+            kd = tap >> 2;
+            kh = (tap >> 1) & 1;
+            kw = tap & 1;
+          } else {
+            kd = tap / 9;
+            kh = (tap / 3) % 3;
+            kw = tap % 3;
+          }
         }
         const int zb = d0 + p.in_zoff;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (; kb < kb1; kb += 2) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
             ok = false;
             break;
           }
-          uint8_t* sa = stage_ptr;
+          uint8_t* sa = smem + stage * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kPlanes * Cfg::kABytes;
           mbar_arrive_expect_tx(&full[stage], tx_bytes);
           armed_mask |= 1u << stage;
@@ -819,8 +832,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tma_load_5d(sa + Cfg::kABytes, &maps.a[map], &full[stage], p.cin_pad + chn, x, y, z, c.b);
             tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + kb * KC, brow);
           }
-          if (++chunk == p.cin_chunks) {
-            chunk = 0;
+          for (chunk += 2; chunk >= p.cin_chunks;) {  // two K blocks on
+            chunk -= p.cin_chunks;
             if (p.mode == kConvUp2) {
               kw ^= 1;
               if (kw == 0) {
@@ -835,12 +848,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               }
             }
           }
-          if (++stage == Cfg::kStages) {
-            stage = 0;
+          stage += 2;
+          if (stage >= Cfg::kStages) {
+            stage -= Cfg::kStages;
             phase ^= 1u;
-            stage_ptr = smem;
-          } else {
-            stage_ptr += Cfg::kStageBytes;
           }
         }
         if (!ok) break;
