@@ -183,14 +183,19 @@ struct ConvCfg {
   static constexpr uint32_t kLayout = KC == 64 ? kSwizzle128 : (KC == 32 ? kSwizzle64 : kSwizzle32);
   static constexpr uint32_t kSbo = 8 * KC * 2;  // bytes between 8-row groups
   static constexpr int kPlanes = EXACT ? 2 : 1;
-  static constexpr int kRowsA = TRANS ? 256 : kTileM;  // activation rows per stage
+  static constexpr int kRowsA = TRANS ? 192 : kTileM;  // activation rows per stage (bricks of <= 3 planes)
   static constexpr int kABytes = kRowsA * KC * 2;
   static constexpr int kBBytesRaw = BN * KC * 2;
   static constexpr int kBBytes = ((kBBytesRaw + 1023) / 1024) * 1024;
   static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
-  // Epilogue staging: 2 output + 2 residual buffers of 128 rows x 128 bytes.
+  // Epilogue staging: output + 2 residual buffers of 128 rows x 128 bytes;
+  // 2 output buffers in the voxel-major tile.  The channel-major tile keeps
+  // one (a tile's few planes of stores drain well within its main loop), so
+  // its ring holds a fourth stage: with ~1.2 us per TMA round trip the
+  // bytes in flight bound that pipeline.
   static constexpr int kEpiBufBytes = kTileM * 128;
-  static constexpr int kEpiBytes = 4 * kEpiBufBytes;
+  static constexpr int kOutBufs = TRANS ? 1 : 2;
+  static constexpr int kEpiBytes = (kOutBufs + 2) * kEpiBufBytes;
   // Per-CTA GroupNorm statistics accumulator: [BN][2] FP32 shifted sums
   // (the channel-major tile keeps its sums in registers).
   static constexpr int kStatsBytes = TRANS ? 0 : BN * 8;
@@ -351,7 +356,7 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
   const int n0 = c.nt * BN;
   const bool has_res = !SPLIT && p.residual != nullptr;
   const uint32_t res_bytes = kRowBytes * static_cast<uint32_t>(p.bw * p.bh * p.bd);
-  uint8_t* const res_base = st.epi + 2 * Cfg::kEpiBufBytes;  // residual buffer rb at res_base + rb * kEpiBufBytes
+  uint8_t* const res_base = st.epi + Cfg::kOutBufs * Cfg::kEpiBufBytes;  // residual buffer rb at res_base + rb * kEpiBufBytes
   if (has_res && st.leader) {
     // prefetch the residual of chunk 0 while the tile's MMAs still run
     const int rb = st.rq & 1;
@@ -551,7 +556,7 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
   constexpr uint32_t kBoxBytes = 64 * 128;  // 64 voxels x 64 channels x 2 B
   const uint32_t res_bytes = static_cast<uint32_t>(nboxes) * kBoxBytes;
   const bool has_res = p.residual != nullptr;
-  uint8_t* const res_base = st.epi + 2 * Cfg::kEpiBufBytes;
+  uint8_t* const res_base = st.epi + Cfg::kOutBufs * Cfg::kEpiBufBytes;
   auto prefetch_res = [&](int pl, int rb) {
     mbar_arrive_expect_tx(&st.res_full[rb], res_bytes);
     for (int bx = 0; bx < nboxes; ++bx)
@@ -580,9 +585,9 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
   const uint32_t box_off = static_cast<uint32_t>(ch >> 6) * kBoxBytes;
 #pragma unroll 1
   for (int pl = 0; pl < p.bd; ++pl) {
-    uint8_t* ob = st.epi + (st.oq & 1) * Cfg::kEpiBufBytes;
+    uint8_t* ob = st.epi;
     if (st.leader) {
-      bulk_wait_group_read<1>();  // the stores issued two planes ago have read this buffer
+      bulk_wait_group_read<0>();  // the previous plane's stores have read the staging buffer
       if (has_res && pl + 1 < p.bd) prefetch_res(pl + 1, (st.rq + 1) & 1);
     }
     named_barrier(1, 128);
@@ -674,7 +679,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi = smem + Cfg::kStages * Cfg::kStageBytes;  // out[2] | res[2], 1024-aligned
+  uint8_t* epi = smem + Cfg::kStages * Cfg::kStageBytes;  // out[kOutBufs] | res[2], 1024-aligned
   uint64_t* full = reinterpret_cast<uint64_t*>(epi + Cfg::kEpiBytes);
   uint64_t* empty = full + Cfg::kStages;
   uint64_t* acc_full = empty + Cfg::kStages;
@@ -1192,7 +1197,7 @@ bool conv_trans_enabled() {
 // Tile-selection overrides for measurements (read on every plan): LDB_CONV_BN
 // (64 or 128) replaces the 256-column tile where the packed weight rows are
 // the same (out_channels a multiple of 256); LDB_CONV_SPLITS fixes the
-// split-K factor; LDB_CONV_TRANS_BD (1..4) the brick depth of the
+// split-K factor; LDB_CONV_TRANS_BD (1..3) the brick depth of the
 // channel-major tile.  Unset or 0: the planner's choice.
 int env_int(const char* name) {
   const char* v = std::getenv(name);
@@ -1321,8 +1326,9 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   plan->cin_pad = cin_pad;
   // Channel-major tile for 64 / 128 output channels when the grid needs no
   // split-K: the MMA runs as 128 (channels) x 64*bd (voxels of a bd x 8 x 8
-  // brick), the efficient 128 x 256 shape at bd = 4 where a 128-channel
-  // voxel-major tile would run 128 x 128.  bd minimises waves x tile size.
+  // brick, bd <= 3: a 192-row stage leaves room for a four-stage ring) where
+  // a 128-channel voxel-major tile would run 128 x 128.  bd minimises waves x
+  // tile size.
   // (64-channel K blocks only: with 16 / 32 input channels per block the
   // per-block overhead dominates and the voxel-major tile is faster.  3x3x3
   // kernels only: a pointwise conv has too few K blocks per tile to hide the
@@ -1333,9 +1339,9 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     const long long th = (gh + 7) / 8, tw = (gw + 7) / 8;
     int best_bd = 1;
     long long best_cost = -1;
-    const int force_bd = env_int("LDB_CONV_TRANS_BD");  // tuning override, 1..4
-    for (int cand = 1; cand <= 4; ++cand) {
-      if (force_bd >= 1 && force_bd <= 4 && cand != force_bd) continue;
+    const int force_bd = env_int("LDB_CONV_TRANS_BD");  // tuning override, 1..3
+    for (int cand = 1; cand <= 3; ++cand) {
+      if (force_bd >= 1 && force_bd <= 3 && cand != force_bd) continue;
       const long long tiles = static_cast<long long>(B) * ((gd + cand - 1) / cand) * th * tw * p.parities;
       const long long cost = ((tiles + sms - 1) / sms) * (64LL * cand + 64);
       if (best_cost < 0 || cost <= best_cost) {
