@@ -39,8 +39,7 @@ namespace ldb {
 
 namespace {
 
-constexpr int kConvWarps = 7;  // warps 0 and 6 TMA producers, warp 1 MMA, warps 2-5 epilogue
-constexpr int kConvThreads = 32 * kConvWarps;
+// Warps: 0 and 6 .. 4 + P the P TMA producers, 1 the MMA issuer, 2-5 the epilogue.
 constexpr int kTileM = 128;
 
 struct TileCoord {
@@ -201,6 +200,10 @@ struct ConvCfg {
   static constexpr int kStatsBytes = TRANS ? 0 : BN * 8;
   static constexpr int kStagesRaw = (225 * 1024 - kEpiBytes - 2048 - kStatsBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  // Producer warps taking K blocks in turn: four where K blocks are small
+  // (16 / 32 channels: the MMA issuer keeps up with more), else two.
+  static constexpr int kProducers = KC < 64 && kStages >= 4 ? 4 : 2;
+  static constexpr int kThreads = 32 * (5 + kProducers);
   // Two accumulator chains (even / odd K steps, added in the epilogue): the
   // tensor pipe overlaps MMAs into different accumulators but serialises
   // successive MMAs into one, which at N <= 128 leaves it idle about half of
@@ -673,7 +676,7 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
 }
 
 template <int KC, int BN, bool EXACT, bool TRANS>
-__global__ void __launch_bounds__(kConvThreads, 1)
+__global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
     conv3d_tc_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ CUtensorMap wmap,
                      const ConvParams p, unsigned int* status) {
   using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
@@ -744,21 +747,23 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t a_box_bytes = static_cast<uint32_t>(KC * 2 * p.bw * p.bh * p.bd);
   const uint32_t tx_bytes = Cfg::kPlanes * (a_box_bytes + static_cast<uint32_t>(Cfg::kBBytesRaw));
 
-  if (warp == 0 || warp == kConvWarps - 1) {
+  if (warp == 0 || warp >= 6) {
     // ------------------------------------------------------------ producers
-    // Two producer warps (0 and the last) take alternate K blocks of the
-    // CTA's sequence (flattened over its tiles): K block j goes to producer
-    // j % 2 and to stage j % kStages.  Per K block one thread waits for the
-    // stage, arms it and issues the loads, a path of some hundred cycles of
-    // dependent latency that sets the pipeline's rate when it runs on one
-    // thread; two run it side by side.
+    // P producer warps (0, then 6 and up) take the K blocks of the CTA's
+    // sequence (flattened over its tiles) in turn: K block j goes to
+    // producer j % P and to stage j % kStages.  Per K block one thread waits
+    // for the stage, arms it and issues the loads, a path of some hundred
+    // cycles of dependent latency that sets the pipeline's rate when it runs
+    // on one thread; P run it side by side.
+    constexpr int P = Cfg::kProducers;
+    static_assert(P <= Cfg::kStages, "a producer's next stage must differ from its current one");
     if (lane == 0) {
-      const int pid = warp == 0 ? 0 : 1;
+      const int pid = warp == 0 ? 0 : warp - 5;
       int stage = pid;
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_parity = 0;
       bool waited = false;
-      int jt = 0;  // sequence index of the current tile's first K block
+      int jt = 0;  // sequence index of the current tile's first K block, mod P
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord c = decode_tile(p, t);
         const int kb0 = c.ks * p.kb_per_split;
@@ -766,12 +771,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
         const int pd = c.par >> 2, ph = (c.par >> 1) & 1, pw = c.par & 1;
         const int brow = c.par * p.wrows_per_parity + c.nt * BN;
-        int kb = kb0 + ((jt + pid) & 1);  // this producer's first K block of the tile
-        jt += kb1 - kb0;
+        int kb = kb0 + (pid - jt + P) % P;  // this producer's first K block of the tile
+        jt = (jt + kb1 - kb0) % P;
         if (kb >= kb1) continue;
         bool ok = true;
         // Tap digits (kd, kh, kw; for the folded up-conv the bits td, th, tw)
-        // and channel chunk of kb, then advanced two K blocks at a time by
+        // and channel chunk of kb, then advanced P K blocks at a time by
         // counters (no division per K block).  The weight column of K block kb
         // is kb * KC (tap * cin_pad + chunk * KC).
         int chunk, kd, kh, kw;
@@ -789,7 +794,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
         }
         const int zb = d0 + p.in_zoff;
-        for (; kb < kb1; kb += 2) {
+        for (; kb < kb1; kb += P) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
             ok = false;
             break;
@@ -837,7 +842,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tma_load_5d(sa + Cfg::kABytes, &maps.a[map], &full[stage], p.cin_pad + chn, x, y, z, c.b);
             tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + kb * KC, brow);
           }
-          for (chunk += 2; chunk >= p.cin_chunks;) {  // two K blocks on
+          for (chunk += P; chunk >= p.cin_chunks;) {  // P K blocks on
             chunk -= p.cin_chunks;
             if (p.mode == kConvUp2) {
               kw ^= 1;
@@ -853,7 +858,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               }
             }
           }
-          stage += 2;
+          stage += P;
           if (stage >= Cfg::kStages) {
             stage -= Cfg::kStages;
             phase ^= 1u;
@@ -1153,7 +1158,7 @@ int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wm
                                          "conv smem attribute");
     if (rc != LDB_OK) return rc;
   }
-  int rc = launch_kernel(kernel, dim3(grid), dim3(kConvThreads), smem, stream, "conv3d launch", maps, wmap, p,
+  int rc = launch_kernel(kernel, dim3(grid), dim3(Cfg::kThreads), smem, stream, "conv3d launch", maps, wmap, p,
                          device_status_ptr());
   if (rc != LDB_OK) return rc;
   if (p.k_splits > 1) {
