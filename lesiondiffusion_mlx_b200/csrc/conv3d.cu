@@ -3,9 +3,9 @@
 // GEMM view: rows M are output voxels (source voxels for the folded 2x
 // upsampling conv), columns N are output channels, and K runs over
 // (tap, input-channel block).  Nothing is im2col'ed: for each K block a
-// producer warp (two take alternate K blocks) issues one 5-D TMA load of a
-// bd x bh x bw brick of voxels x
-// KC channels of the NDHWC activation, offset by the tap; TMA's out-of-bounds
+// producer warp (two or four take the K blocks in turn) issues one 5-D TMA
+// load of a bd x bh x bw brick of voxels x KC channels of the NDHWC
+// activation, offset by the tap; TMA's out-of-bounds
 // zero fill supplies the padding.  Weights are packed K-major
 // [parity][Cout][tap][Cin] and loaded as 2-D TMA tiles.  A single thread of
 // the MMA warp issues tcgen05.mma (M=128, N=BN, K=16) into a double-buffered
