@@ -36,7 +36,7 @@ extern "C" {
 
 typedef struct CUstream_st* ldb_stream_t; /* binary compatible with cudaStream_t */
 
-#define LDB_ABI_VERSION 1
+#define LDB_ABI_VERSION 2
 
 enum {
   LDB_OK = 0,
@@ -61,7 +61,8 @@ enum {
 
 enum { LDB_ACT_NONE = 0, LDB_ACT_GELU = 1 };
 
-/* Library ABI version (LDB_ABI_VERSION). */
+/* Library ABI version (LDB_ABI_VERSION).  Version 2 added
+ * ldb_conv_desc.struct_size as the descriptor's first field. */
 LDB_API int ldb_version(void);
 
 /* Number of kernels this library has launched (or recorded into a CUDA
@@ -92,6 +93,12 @@ LDB_API int ldb_device_status(unsigned int* status, int reset);
  * doubled (UP2).
  * ---------------------------------------------------------------------- */
 typedef struct {
+  /* sizeof(ldb_conv_desc) as the caller compiled it.  Every entry point that
+   * takes a descriptor rejects any other value with LDB_ERR_INVALID, so a
+   * binding written against another layout of this struct fails cleanly
+   * instead of reading past what it passed.  Bindings that mirror the struct
+   * (ctypes, cffi) set it to their own structure size. */
+  int struct_size;
   int batch, depth, height, width; /* input grid */
   int in_channels;                 /* channels read from x (per plane) */
   int x_ld;                        /* channel stride of x, multiple of 8 */
@@ -166,7 +173,10 @@ LDB_API int ldb_group_norm_affine(ldb_stream_t stream, const void* x1, int c1, i
  * batch * channels must not exceed 524288; larger calls fail with
  * LDB_ERR_SHAPE.  Performs no cudaMalloc / cudaFree.  The first call on a
  * device looks up the array's device address (make it before any stream
- * capture).  All calls share the array: calls that overlap on the GPU race.
+ * capture).  Under lazy module loading (the CUDA 12 default) the driver
+ * places the array in device memory only at that first call or at the first
+ * launch of another GroupNorm kernel of the library: make the first call
+ * before reserving all device memory, or set CUDA_MODULE_LOADING=EAGER.  All calls share the array: calls that overlap on the GPU race.
  * Same arguments and results as ldb_group_norm_affine without the workspace. */
 LDB_API int ldb_group_norm_affine_noalloc(ldb_stream_t stream, const void* x1, int c1, int ld1, const void* x2,
                                           int c2, int ld2, int dtype, int batch, int voxels, int groups,

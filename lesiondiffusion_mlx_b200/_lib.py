@@ -29,9 +29,10 @@ class LdbError(RuntimeError):
 
 
 class ConvDesc(ctypes.Structure):
-    """Mirror of ``ldb_conv_desc``."""
+    """Mirror of ``ldb_conv_desc``; ``struct_size`` is filled in on construction."""
 
     _fields_ = [
+        ("struct_size", ctypes.c_int),
         ("batch", ctypes.c_int),
         ("depth", ctypes.c_int),
         ("height", ctypes.c_int),
@@ -49,6 +50,10 @@ class ConvDesc(ctypes.Structure):
         ("depth_halo", ctypes.c_int),
         ("clock", ctypes.c_void_p),
     ]
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.struct_size = ctypes.sizeof(ConvDesc)
 
 
 _P = ctypes.c_void_p

@@ -1217,6 +1217,11 @@ struct ConvPlan {
 
 int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   if (!d) return fail(LDB_ERR_INVALID, "conv descriptor is null");
+  if (d->struct_size != static_cast<int>(sizeof(ldb_conv_desc)))
+    return fail(LDB_ERR_INVALID,
+                "conv descriptor struct_size %d != %d: the caller's ldb_conv_desc layout is not this library's "
+                "(ABI version %d)",
+                d->struct_size, static_cast<int>(sizeof(ldb_conv_desc)), LDB_ABI_VERSION);
   const int B = d->batch, D = d->depth, H = d->height, W = d->width;
   if (B <= 0 || D <= 0 || H <= 0 || W <= 0) return fail(LDB_ERR_SHAPE, "conv input extents must be positive");
   if (d->in_channels <= 0 || d->out_channels <= 0) return fail(LDB_ERR_SHAPE, "conv channels must be positive");

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.ldb_version() == 1
+    assert lib.ldb_version() == 2
 
 
 def test_errors_are_reported_without_a_device():
@@ -46,6 +46,51 @@ def test_errors_are_reported_without_a_device():
     desc.mode = 9
     with pytest.raises(_lib.LdbError, match="unknown conv mode"):
         _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(size))
+
+
+def test_conv_descriptor_of_another_layout_is_rejected():
+    """A binding that mirrors an older or shorter ``ldb_conv_desc`` (no
+    ``struct_size`` first field, or a struct that stops before ``clock``) gets
+    LDB_ERR_INVALID from every descriptor entry point instead of a launch that
+    reads past the struct it passed."""
+    from lesiondiffusion_mlx_b200 import _lib
+
+    good = _lib.ConvDesc(batch=1, depth=2, height=2, width=2, in_channels=16, x_ld=16, out_channels=8, out_ld=8,
+                         res_ld=8, mode=0, exact=0, out_dtype=0, act=0, output_scale=1.0)
+    size = ctypes.c_size_t(0)
+    _lib.call("ldb_conv3d_workspace_size", ctypes.byref(good), ctypes.byref(size))
+    assert good.struct_size == ctypes.sizeof(_lib.ConvDesc) == 72
+
+    class ShortDesc(ctypes.Structure):
+        # the version-1 layout: no struct_size, and it ends at depth_halo
+        _fields_ = [(n, ctypes.c_int) for n in ("batch", "depth", "height", "width", "in_channels", "x_ld",
+                                                "out_channels", "out_ld", "res_ld", "mode", "exact", "out_dtype",
+                                                "act")] + [("output_scale", ctypes.c_float), ("depth_halo", ctypes.c_int)]
+
+    # a padded buffer keeps the library's read of the full struct inside our own memory
+    buf = (ctypes.c_char * ctypes.sizeof(_lib.ConvDesc))()
+    short = ShortDesc.from_buffer(buf)
+    short.batch, short.depth, short.height, short.width = 1, 2, 2, 2
+    short.in_channels, short.x_ld, short.out_channels, short.out_ld, short.res_ld = 16, 16, 8, 8, 8
+    short.output_scale = 1.0
+    lib = _lib.library()
+    rows, k = ctypes.c_int(0), ctypes.c_int(0)
+    stats_host = (ctypes.c_double * 2)()  # non-null, so the descriptor check is what fails
+    stats_ptr = ctypes.cast(stats_host, ctypes.c_void_p)
+    for name, args in (("ldb_conv3d_workspace_size", (ctypes.byref(size),)),
+                       ("ldb_conv3d_weight_rows", (ctypes.byref(rows), ctypes.byref(k))),
+                       ("ldb_conv3d_fwd", (None, None, None, None, None, None, None, 0)),
+                       ("ldb_conv3d_fwd_gn_stats", (None, None, None, None, None, None, stats_ptr, None, 0))):
+        fn = getattr(lib, name)
+        if name.startswith("ldb_conv3d_fwd"):
+            rc = fn(None, ctypes.cast(buf, ctypes.POINTER(_lib.ConvDesc)), *args)
+        else:
+            rc = fn(ctypes.cast(buf, ctypes.POINTER(_lib.ConvDesc)), *args)
+        assert rc == -1, name  # LDB_ERR_INVALID
+        assert b"struct_size" in lib.ldb_last_error(), name
+    good.struct_size = 64
+    with pytest.raises(_lib.LdbError, match="struct_size 64"):
+        _lib.call("ldb_conv3d_workspace_size", ctypes.byref(good), ctypes.byref(size))
 
 
 @pytest.mark.parametrize("cin,cout,exact,rows,k", [(128, 128, False, 128, 27 * 128), (8, 8, False, 16, 27 * 16),
