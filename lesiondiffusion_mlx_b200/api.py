@@ -175,10 +175,15 @@ def resize_nearest(x: torch.Tensor, shape: tuple[int, ...], *, mx=None) -> torch
     """NCDHW nearest resize with source index floor(i * in / out) (_spatial.py:60-69)."""
     if len(shape) != 3:
         raise ValueError("LesionDiffusion nearest resizing needs three spatial axes")
-    esz = x.element_size()
-    pad = max(1, 8 // esz)
-    out = ops.resize_nearest(_to_ndhwc(x, pad), tuple(int(s) for s in shape))
-    return _to_ncdhw(out)
+    if x.ndim != 5:
+        raise ValueError("resize_nearest expects NCDHW input")
+    # rows are copied whole, so resize the channel-padded buffer (rows a
+    # multiple of 8 bytes) and drop the padding afterwards
+    c = int(x.shape[1])
+    padded = _to_ndhwc(x, max(1, 8 // x.element_size()))
+    full = padded.as_strided((*padded.shape[:-1], padded.stride(-2)), padded.stride())
+    out = ops.resize_nearest(full, tuple(int(s) for s in shape))
+    return _to_ncdhw(out[..., :c])
 
 
 def piecewise_ct(array: torch.Tensor, mx=None, *, inverse: bool = False) -> torch.Tensor:
