@@ -226,20 +226,26 @@ class OracleVq(OracleLayers):
 
     SCALE = 0.25
 
-    def __init__(self, weights, *, scaled: bool = False, **kw):
+    def __init__(self, weights, *, scaled: bool = False, groups: int = 16, **kw):
         super().__init__(weights, **kw)
         self.scaled = scaled
+        self.groups = groups
+        names = list(weights)
+        # Decoder levels run from the highest index down (mlx_model.py:813-817); the
+        # reference checkpoint has levels 2, 1, 0 with one upsample after level 1.
+        self.levels = sorted({int(n.split(".")[2]) for n in names if n.startswith("decoder.up.")}, reverse=True)
+        self.blocks = {lvl: sorted({int(n.split(".")[4]) for n in names
+                                    if n.startswith(f"decoder.up.{lvl}.block.")}) for lvl in self.levels}
 
-    def residual(self, x: torch.Tensor, key: str) -> torch.Tensor:
-        """mlx_model.py:720-727 (ScaledVqDecoder.norm_silu_conv for the scaled variant)."""
-        eps1 = 1e-6
-        if self.scaled and key.startswith("decoder.up.0.block."):
-            eps1 *= self.SCALE ** 2
-        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=16, eps=eps1)
+    def residual(self, x: torch.Tensor, key: str, *, scaled: bool = False) -> torch.Tensor:
+        """mlx_model.py:720-727 (ScaledVqDecoder.norm_silu_conv for the scaled variant:
+        blocks after the upsample take eps * s^2 and scale their output, _scaled_vq.py:75-118)."""
+        eps1 = 1e-6 * (self.SCALE ** 2 if scaled else 1.0)
+        h = self.norm_silu_conv(x, key + ".norm1", key + ".conv1", groups=self.groups, eps=eps1)
         if key + ".nin_shortcut.weight" in self.w:
             x = self.conv(x, key + ".nin_shortcut", padding=0)
-        scale = self.SCALE if (self.scaled and key.startswith("decoder.up.0.block.")) else 1.0
-        return self.norm_silu_conv(h, key + ".norm2", key + ".conv2", groups=16, eps=1e-6, residual=x,
+        scale = self.SCALE if scaled else 1.0
+        return self.norm_silu_conv(h, key + ".norm2", key + ".conv2", groups=self.groups, eps=1e-6, residual=x,
                                    output_scale=scale)
 
     def encode(self, x: torch.Tensor) -> torch.Tensor:
@@ -264,14 +270,16 @@ class OracleVq(OracleLayers):
         x = self.conv(x, "decoder.conv_in")
         x = self.residual(x, "decoder.mid.block_1")
         x = self.residual(x, "decoder.mid.block_2")
-        for level in reversed(range(3)):
-            for block in range(2):
-                x = self.residual(x, f"decoder.up.{level}.block.{block}")
-            if level == 1:
+        upsampled = False
+        for level in self.levels:
+            for block in self.blocks[level]:
+                x = self.residual(x, f"decoder.up.{level}.block.{block}", scaled=self.scaled and upsampled)
+            if f"decoder.up.{level}.upsample.conv.weight" in self.w:
                 scale = self.SCALE if self.scaled else 1.0
-                x = self.upsample_conv(x, "decoder.up.1.upsample.conv", output_scale=scale)
+                x = self.upsample_conv(x, f"decoder.up.{level}.upsample.conv", output_scale=scale)
+                upsampled = True
         eps = 1e-6 * (self.SCALE ** 2 if self.scaled else 1.0)
-        return self.norm_silu_conv(x, "decoder.norm_out", "decoder.conv_out", groups=16, eps=eps)
+        return self.norm_silu_conv(x, "decoder.norm_out", "decoder.conv_out", groups=self.groups, eps=eps)
 
 
 def torch_weights(arrays: dict, dtype: torch.dtype) -> dict[str, torch.Tensor]:
