@@ -748,7 +748,11 @@ int ldb_layer_norm(cudaStream_t stream, const void* x, int x_ld, const float* ga
 // device scratch (g_gn_noalloc_scratch) instead of a caller workspace.  For
 // callers that cannot allocate device memory at call time.  The first call
 // on a device looks up the scratch address (make it before any stream
-// capture).  Calls share the scratch, so calls that overlap on the GPU
+// capture).  With lazy module loading (the CUDA 12 default) that lookup, or
+// the first launch of any kernel of this file, is also when the driver loads
+// this file's module and places the 4 MiB array in device memory: make the
+// first call before the caller reserves all of the device's memory, or run
+// the process with CUDA_MODULE_LOADING=EAGER.  Calls share the scratch, so calls that overlap on the GPU
 // (different streams, or different host threads) race; each call fully
 // writes every partial it reads, so nothing needs clearing between calls.
 int ldb_group_norm_affine_noalloc(cudaStream_t stream, const void* x1, int c1, int ld1, const void* x2, int c2,
@@ -788,14 +792,11 @@ int ldb_group_norm_affine_noalloc(cudaStream_t stream, const void* x1, int c1, i
     if (rc != LDB_OK) return rc;
   }
   const int chunk_voxels = (voxels + nchunks - 1) / nchunks;
-  gn_partial_kernel<<<dim3(nchunks, batch), threads, smem, stream>>>(s, voxels, chunk_voxels, partials, nchunks);
-  count_launch();
-  rc = check_cuda(cudaGetLastError(), "gn_partial (noalloc) launch");
+  rc = launch_kernel(gn_partial_kernel, dim3(nchunks, batch), dim3(threads), smem, stream,
+                     "gn_partial (noalloc) launch", s, voxels, chunk_voxels, partials, nchunks);
   if (rc != LDB_OK) return rc;
-  gn_finalize_kernel<<<batch * groups, 256, 0, stream>>>(s, voxels, partials, nchunks, groups, gamma, beta, eps,
-                                                         affine);
-  count_launch();
-  return check_cuda(cudaGetLastError(), "gn_finalize (noalloc) launch");
+  return launch_kernel(gn_finalize_kernel, dim3(batch * groups), dim3(256), 0, stream, "gn_finalize (noalloc) launch",
+                       s, voxels, static_cast<const float2*>(partials), nchunks, groups, gamma, beta, eps, affine);
 }
 
 }  // extern "C"

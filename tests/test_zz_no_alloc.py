@@ -40,7 +40,12 @@ def _noalloc_affine(x1: torch.Tensor, x2: torch.Tensor | None, gamma: torch.Tens
 def test_noalloc_group_norm_matches_workspace_entry_point_twice(cuda_device, dtype):
     from lesiondiffusion_mlx_b200 import ops
 
-    cases = [((2, 6, 10, 12, 256), None, 32), ((1, 4, 20, 20, 512), 256, 32)]
+    # The last two cases hold batch x 1024 channels over 20480 voxels: the fixed
+    # array cannot take one partial per planned chunk there, so the entry point
+    # reduces the chunk count (512 and 256 chunks instead of the workspace
+    # path's count) and the sums are formed over longer chunks.
+    cases = [((2, 6, 10, 12, 256), None, 32), ((1, 4, 20, 20, 512), 256, 32), ((1, 16, 32, 40, 1024), None, 32),
+             ((2, 16, 32, 40, 1024), 512, 32)]
     for i, (shape, split, groups) in enumerate(cases):
         rng = np.random.default_rng(40 + i)
         x = torch.from_numpy((rng.normal(size=shape) * 2 + 0.5).astype(np.float32)).to(dtype).to(cuda_device)
