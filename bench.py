@@ -13,8 +13,18 @@ Multi-GPU: one process per GPU (torchrun); every rank runs its own
 trajectory replica (seeds are data-parallel, no collective on the data
 path), timing is the max over ranks, ``value`` is the steps/s of all ranks.
 
+Besides the timed K steps the line carries: ``trajectory`` (one full
+200-step DDIM trajectory plus the config-4a decode to HU, the north star's
+"generation under 10 s" unit), ``decode_4b`` (the config-4b VQ decode:
+unsharded at N = 1, depth-sharded over the N ranks with NCCL halo exchange
+and GroupNorm all-reduces at N > 1), the conv ``roofline`` against the
+measured burst bf16 peak (the step is milliseconds long), and at N = 1 the
+CPU baseline.  Clocks are sampled from the start of the timed steps to the
+end of the trajectory.
+
 ``--impl reference`` times the CPU restatement of the reference arithmetic
-(``oracle/``, the reference itself is MLX/Metal-only) on the host cores.
+(``oracle/``, the reference itself is MLX/Metal-only) on the host cores, on
+the same workload ``config``.
 """
 
 from __future__ import annotations
@@ -56,7 +66,7 @@ def linet_alphas() -> np.ndarray:
 
 
 class ClockSampler:
-    """Sample nvidia-smi SM clocks and throttle reasons every 200 ms in a thread."""
+    """Sample nvidia-smi SM clocks and throttle reasons every 100 ms in a thread."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -71,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except (OSError, ValueError):
@@ -124,6 +134,25 @@ def dist_setup(n: int):
 
 
 _ORACLE: dict = {}
+
+
+def config3_param_bytes() -> int:
+    """f16 bytes of the config-3 UNet's weights."""
+    from lesiondiffusion_mlx_b200 import workloads
+
+    raw = workloads.unet_weights(workloads.CONFIG3, 8, 8, 768, seed=0, shapes_only=True)
+    return int(sum(v.size * 2 for v in raw.values()))
+
+
+def workload_config(world: int) -> dict:
+    """The workload both arms report (identical dicts, so the two lines compare)."""
+    return {
+        "workload": "config3-unet-ddim-step", "latent": [1, 8, 32, 40, 40], "context": [1, 77, 768],
+        "global_batch": world, "parallelism": f"replicas x{world} (independent seeds)",
+        "l2": f"per-step working set > L2: {config3_param_bytes() / 1e6:.0f} MB of weights streamed every step",
+        "graph": "one CUDA graph per step (UNet forward + fused DDIM update)",
+        "schedule": "DDIM 200 steps, eta 1, real LINet alphas_cumprod",
+    }
 
 
 def cpu_step_time(depth: int, threads: int) -> tuple[float, dict]:
@@ -185,19 +214,30 @@ def run_reference(args, rank: int) -> None:
     times = [cpu_step_time(depth, threads)[0] for _ in range(args.steps)]
     per_step_full = sum(times) / len(times) * 32 / depth
     value = 1.0 / per_step_full
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_step_full * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 (storage; FP32/FP64 CPU arithmetic)", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "config3-unet-ddim-step", "latent": [1, 8, 32, 40, 40], "global_batch": 1,
-                   "parallelism": "host cores"},
+        "config": workload_config(max(world, args.gpus)),
+        "execution": f"one replica on {threads} host cores (rank 0 only)",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"each step: one oracle UNet step + DDIM update on a 1x8x{depth}x40x40 depth "
                                    f"crop, scaled by 32/{depth}; the reference is MLX/Metal-only and cannot run here"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _max_over_ranks(value: float, world: int, device) -> float:
+    if world <= 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def main() -> None:
@@ -211,16 +251,18 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
-    from lesiondiffusion_mlx_b200 import _lib, instrument, workloads
-    from lesiondiffusion_mlx_b200.networks import LdmUnetB200
+    from lesiondiffusion_mlx_b200 import _lib, instrument, ops, vq_bench, workloads
+    from lesiondiffusion_mlx_b200.networks import LdmUnetB200, VqDecoderB200
     from lesiondiffusion_mlx_b200.sampling import DdimSampler, PreparedSampler
 
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     cfg = workloads.CONFIG3
     raw = workloads.unet_weights(cfg, 8, 8, 768, seed=100)
     weights = {k: torch.from_numpy(v).to(torch.float16) for k, v in raw.items()}
-    param_bytes = sum(v.numel() * 2 for v in weights.values())
     unet = LdmUnetB200(weights, cfg, device=device)
     inp = workloads.config3_inputs(seed=101 + rank)
     cache = unet.prepare_context(torch.from_numpy(inp["context"]).to(device))
@@ -232,13 +274,16 @@ def main() -> None:
     init = torch.randn(prepared.state.x.shape, generator=gen, device=device)
     noise = torch.randn(prepared.state.noise.shape, generator=gen, device=device)
     prepared.begin(init, noise)
+    decoder = VqDecoderB200({k: torch.from_numpy(v) for k, v in workloads.config4_decoder_weights().items()},
+                            device=device, groups=32)
+    latent = torch.zeros((1, 32, 40, 40, 8), dtype=torch.float16, device=device)
 
     # Capture one step (UNet + DDIM update + step advance) twice: a plain graph
     # for the timed region, and a copy replayed afterwards for the per-kernel
-    # breakdown.  In the copy every conv launch times itself from the device
-    # clock (its first CTA past the dependency wait to its last CTA or split-K
-    # reduce finishing; no node is added to its path), and the other kernels
-    # have CUDA event pairs around them (whose nodes add gaps).
+    # breakdown.  In the copy every conv and attention launch times itself from
+    # the device clock (its first CTA past the dependency wait to its last CTA
+    # or split-K reduce finishing; no node is added to its path), and the other
+    # kernels have CUDA event pairs around them (whose nodes add gaps).
     timer = instrument.KernelTimer(device_clock=True)
     timer.arm(device)
     prepared._step()  # eager warm-up (first-use setup outside capture)
@@ -253,23 +298,19 @@ def main() -> None:
         prepared._step()
     prepared.begin(init, noise)
 
-    def reset_if_needed(done: int) -> None:
-        if done and done % sampler.steps == 0:
-            prepared.begin(init, noise)
-
     stream = torch.cuda.current_stream(device)
     done = 0
     for _ in range(args.warmup):
-        reset_if_needed(done)
+        if done and done % sampler.steps == 0:
+            prepared.begin(init, noise)
         graph.replay()
         done += 1
+    decoder.decode(latent, quantize=False)  # warm-up of the decoder (first-use packing)
     torch.cuda.synchronize()
     prepared.begin(init, noise)
     done = 0
 
-    if world > 1:
-        import torch.distributed as dist
-
+    if dist is not None:
         dist.barrier()
     clocks = ClockSampler(device.index)
     clocks.start()
@@ -286,20 +327,40 @@ def main() -> None:
         done += 1
     end.record(stream)
     torch.cuda.synchronize()
-    clock_info = clocks.stop()
     elapsed_ms = start.elapsed_time(end)
+
+    # One whole generation, the north star's unit: a 200-step DDIM trajectory
+    # from the initial state, then the config-4a decode of [latent | mask] to
+    # HU (1 x 128 x 160 x 160).  Same clocks record.
+    prepared.begin(init, noise)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_mid = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(sampler.steps):
+        graph.replay()
+    t_mid.record(stream)
+    latent[..., :7].copy_(prepared.state.x)
+    latent[..., 7].copy_(prepared.state.mask)
+    hu = ops.hu_map(decoder.decode(latent, quantize=False))
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    trajectory_ms = t_start.elapsed_time(t_mid)
+    decode_ms = t_mid.elapsed_time(t_end)
+    hu_finite = bool(torch.isfinite(hu).all().item())
+    del hu
+
     prepared.begin(init, noise)
     for _ in range(3):
         timer.reset()
         timed_graph.replay()
     torch.cuda.synchronize()
     kernel = timer.summary()
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([elapsed_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms = _max_over_ranks(elapsed_ms, world, device)
+    trajectory_ms = _max_over_ranks(trajectory_ms, world, device)
+    decode_ms = _max_over_ranks(decode_ms, world, device)
+    if dist is not None:
         dist.barrier()
     ms_per_step = elapsed_ms / args.steps
     value = world * args.steps / (elapsed_ms / 1e3)
@@ -310,7 +371,7 @@ def main() -> None:
     host_noise = noise[0].cpu().pin_memory()
     host_out = torch.empty(prepared.state.x.shape, dtype=torch.float32).pin_memory()
     prepared.begin(init, noise)
-    if world > 1:
+    if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     e_start = torch.cuda.Event(enable_timing=True)
@@ -325,13 +386,15 @@ def main() -> None:
         host_out.copy_(prepared.state.x, non_blocking=True)
     e_end.record(stream)
     torch.cuda.synchronize()
-    e_ms = e_start.elapsed_time(e_end)
-    if world > 1:
-        t = torch.tensor([e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item())
+    e_ms = _max_over_ranks(e_start.elapsed_time(e_end), world, device)
     e_value = world * e_steps / (e_ms / 1e3)
     status = _lib.device_status(reset=True)
+    del graph, timed_graph, prepared, unet, decoder, latent
+    torch.cuda.empty_cache()
+
+    # Config 4b: unsharded on one GPU, depth-sharded over all ranks at N > 1
+    # (every rank takes part; collectives in the same order on every rank).
+    decode_4b = vq_bench.measure("4b", device, steps=2, warmup=1, dist=dist)
 
     if rank == 0:
         peaks = {}
@@ -342,48 +405,55 @@ def main() -> None:
         attn = kernel.get("attention", {"ms": float("nan"), "flops": 0.0, "launches": 0})
         conv_tflops = conv["flops"] / (conv["ms"] * 1e-3) / 1e12 if conv["ms"] else None
         attn_tflops = attn["flops"] / (attn["ms"] * 1e-3) / 1e12 if attn["ms"] else None
-        peak = peaks.get("bf16_tflops_sustained", 1404.7) if peaks else 1400.0
-        peak_burst = peaks.get("bf16_tflops", 1674.7) if peaks else 1590.0
+        # The step is a few milliseconds and the timed region well under a second,
+        # so kernels run at burst clocks: the burst peak is the denominator.
+        peak_burst = peaks.get("bf16_tflops", 1590.0)
+        peak_sustained = peaks.get("bf16_tflops_sustained", 1400.0)
+        peak_kind = "measured burst bf16 (MEASURED_PEAKS.json)" if peaks else "fallback burst (1.59 PFLOP/s)"
         traffic_file = ROOT / "profiles" / "conv3d_traffic.json"
         traffic = None
         if traffic_file.exists():
             traffic = json.loads(traffic_file.read_text()).get("bytes_per_step")
+        device_clocked = {"conv3d", "attention"}
+        decode_4b["frac_of_burst_per_gpu"] = decode_4b["tflops_per_gpu"] / peak_burst
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights, seeded inputs)",
-            "config": {
-                "workload": "config3-unet-ddim-step", "latent": [1, 8, 32, 40, 40], "context": [1, 77, 768],
-                "global_batch": world, "parallelism": f"replicas x{world} (independent seeds)",
-                "l2": f"per-step working set > L2: {param_bytes / 1e6:.0f} MB of weights streamed every step",
-                "graph": "one CUDA graph per step (UNet forward + fused DDIM update)",
-            },
+            "config": workload_config(world),
             "roofline": {
                 "kernel": "conv3d (tcgen05 implicit GEMM)", "bound": "tensor",
-                "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s",
-                "frac": (conv_tflops / peak) if conv_tflops else None,
-                "peak_kind": "measured sustained bf16 (MEASURED_PEAKS.json)" if peaks else "fallback",
-                "frac_of_burst": (conv_tflops / peak_burst) if conv_tflops else None,
+                "achieved": conv_tflops, "peak": peak_burst, "unit": "TFLOP/s",
+                "frac": (conv_tflops / peak_burst) if conv_tflops else None, "peak_kind": peak_kind,
+                "frac_of_sustained": (conv_tflops / peak_sustained) if conv_tflops else None,
                 "traffic": traffic,
                 "flops_per_step": conv["flops"], "launches_per_step": conv["launches"], "ms_per_step": conv["ms"],
             },
-            "attention": {"achieved_tflops": attn_tflops, "frac": (attn_tflops / peak) if attn_tflops else None,
+            "attention": {"achieved_tflops": attn_tflops, "frac": (attn_tflops / peak_burst) if attn_tflops else None,
                           "flops_per_step": attn["flops"], "ms_per_step": attn["ms"], "launches": attn["launches"]},
             "e2e": {"value": e_value, "unit": UNIT, "h2d_bytes_per_step": int(host_noise.numel() * 4),
                     "d2h_bytes_per_step": int(host_out.numel() * 4)},
-            "kernel_ms_per_step": {k: round(v["ms"], 4) for k, v in sorted(kernel.items())},
+            "trajectory": {
+                "ddim200_s": trajectory_ms / 1e3, "decode_4a_to_hu_s": decode_ms / 1e3,
+                "generation_s": (trajectory_ms + decode_ms) / 1e3, "target_s": 10.0, "hu_finite": hu_finite,
+                "what": "200 DDIM steps from the initial state (graph replays) + config-4a decode of "
+                        "[7 latent channels | mask] to a 1x128x160x160 HU volume, per rank, max over ranks",
+            },
+            "decode_4b": decode_4b,
+            "kernel_ms_per_step": {
+                "device_clock": {k: round(v["ms"], 4) for k, v in sorted(kernel.items()) if k in device_clocked},
+                "cuda_events": {k: round(v["ms"], 4) for k, v in sorted(kernel.items()) if k not in device_clocked},
+                "note": "device_clock spans are exact per launch; cuda_events spans include the event nodes' gaps",
+            },
             "gpu_launches": int(launches_per_step * args.steps),
             "launches_per_step": int(launches_per_step),
             "clocks": clock_info,
             "device_status": status,
         }
-        if not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
-    del graph, timed_graph
-    if world > 1:
-        import torch.distributed as dist
-
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 

@@ -66,44 +66,78 @@ class LocalDepthComm:
 
 
 class DistDepthComm:
-    """One slab per process, neighbours are ranks r - 1 and r + 1 of ``group``."""
+    """One slab per process, neighbours are ranks r - 1 and r + 1 of ``group``.
 
-    def __init__(self, group=None):
+    With ``timed = True`` every exchange and all-reduce is bracketed by CUDA
+    events on the current stream (the time the decode waits for it);
+    ``comm_ms()`` sums the spans recorded so far."""
+
+    def __init__(self, group=None, timed: bool = False):
         import torch.distributed as dist
 
         self.dist = dist
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.timed = timed
+        self._spans: dict[str, list] = {"exchange": [], "all_reduce": []}
+
+    def _span(self, kind: str):
+        if not self.timed:
+            return None
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        self._spans[kind].append((start, end))
+        return end
+
+    def comm_ms(self, reset: bool = True) -> dict[str, float]:
+        """Milliseconds the decode spent in exchanges and all-reduces (synchronizes)."""
+        torch.cuda.synchronize()
+        out = {k: float(sum(s.elapsed_time(e) for s, e in v)) for k, v in self._spans.items()}
+        out.update({k + "_calls": len(v) for k, v in self._spans.items()})
+        if reset:
+            self._spans = {"exchange": [], "all_reduce": []}
+        return out
 
     def _peer(self, r: int) -> int:
         return self.dist.get_global_rank(self.group, r) if self.group is not None else r
 
     def exchange(self, bufs: list[torch.Tensor]) -> None:
         (buf,) = bufs
+        end = self._span("exchange")
         dist = self.dist
         p2p = []
         # Same order on every rank: towards rank - 1 first, then towards rank + 1.
+        # A depth slice of a batch-1 slab buffer is contiguous (whole channel
+        # stride included), so the sends read and the receives write the slab
+        # buffer in place.
         if self.rank > 0:
-            p2p.append(dist.P2POp(dist.isend, buf[:, 1].contiguous(), self._peer(self.rank - 1), self.group))
-            lo = torch.empty_like(buf[:, 0])
-            p2p.append(dist.P2POp(dist.irecv, lo, self._peer(self.rank - 1), self.group))
+            p2p.append(dist.P2POp(dist.isend, _slice(buf, 1), self._peer(self.rank - 1), self.group))
+            p2p.append(dist.P2POp(dist.irecv, _slice(buf, 0), self._peer(self.rank - 1), self.group))
         if self.rank + 1 < self.world:
-            p2p.append(dist.P2POp(dist.isend, buf[:, -2].contiguous(), self._peer(self.rank + 1), self.group))
-            hi = torch.empty_like(buf[:, -1])
-            p2p.append(dist.P2POp(dist.irecv, hi, self._peer(self.rank + 1), self.group))
-        if not p2p:
-            return
-        for req in dist.batch_isend_irecv(p2p):
-            req.wait()
-        if self.rank > 0:
-            buf[:, 0].copy_(lo)
-        if self.rank + 1 < self.world:
-            buf[:, -1].copy_(hi)
+            last = int(buf.shape[1]) - 1
+            p2p.append(dist.P2POp(dist.isend, _slice(buf, last - 1), self._peer(self.rank + 1), self.group))
+            p2p.append(dist.P2POp(dist.irecv, _slice(buf, last), self._peer(self.rank + 1), self.group))
+        if p2p:
+            for req in dist.batch_isend_irecv(p2p):
+                req.wait()
+        if end is not None:
+            end.record()
 
     def all_reduce(self, stats: list[torch.Tensor]) -> None:
         (s,) = stats
+        end = self._span("all_reduce")
         self.dist.all_reduce(s, group=self.group)
+        if end is not None:
+            end.record()
+
+
+def _slice(buf: torch.Tensor, index: int) -> torch.Tensor:
+    """Depth slice ``index`` of a (1, D, H, W, ld) slab buffer, as a contiguous tensor view."""
+    view = buf[:, index]
+    if not view.is_contiguous():
+        raise ValueError("slab buffers must be batch-1 and dense, so that a depth slice is contiguous")
+    return view
 
 
 class _Slab:

@@ -28,10 +28,21 @@ CONFIG3_LATENT = (1, 8, 32, 40, 40)  # (B, C, D, H, W): 7 latent channels + mask
 CONFIG3_CONTEXT = (1, 77, 768)
 
 
-def unet_weights(config: UnetConfig, in_channels: int, out_channels: int, context_dim: int, seed: int
-                 ) -> dict[str, np.ndarray]:
-    """He-normal float32 weights for a UNet of ``config`` (reference state-dict names)."""
-    rng = np.random.default_rng(seed)
+class _ShapeOnly:
+    """A stand-in generator whose draws are zero-stride arrays: the weight
+    dictionary keeps every name and shape without drawing (or storing) values."""
+
+    def standard_normal(self, shape, dtype=np.float32):
+        return np.broadcast_to(np.zeros((), dtype=dtype), shape)
+
+
+def unet_weights(config: UnetConfig, in_channels: int, out_channels: int, context_dim: int, seed: int,
+                 *, shapes_only: bool = False) -> dict[str, np.ndarray]:
+    """He-normal float32 weights for a UNet of ``config`` (reference state-dict names).
+
+    ``shapes_only`` returns read-only zero-stride arrays of the right shapes
+    (for counting parameters without drawing them)."""
+    rng = _ShapeOnly() if shapes_only else np.random.default_rng(seed)
     w: dict[str, np.ndarray] = {}
 
     def conv(key: str, i: int, o: int, k: int = 3) -> None:
