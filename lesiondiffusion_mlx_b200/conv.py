@@ -275,7 +275,8 @@ def conv3d_ndhwc(
     if stats is not None and (stats.dtype != torch.float64 or tuple(stats.shape) != (batch, cout, 2)
                               or not stats.is_contiguous()):
         raise ValueError(f"stats must be a contiguous float64 {(batch, cout, 2)} tensor")
-    desc.clock = instrument.device_clock("conv3d", flops, x.device)
+    label = f"mode{mode} B{batch} {grid[0]}x{grid[1]}x{grid[2]} {cin}->{cout}{' exact' if packed.exact else ''}"
+    desc.clock = instrument.device_clock("conv3d", flops, x.device, label)
     with instrument.maybe_time("conv3d", flops, device_clocked=desc.clock is not None):
         if stats is None:
             _lib.call(

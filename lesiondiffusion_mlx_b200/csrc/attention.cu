@@ -63,11 +63,16 @@ struct AttnCfg {
   static constexpr int kOffK = 2 * kPlanes * kQBytes;
   static constexpr int kStageBytes = 2 * kPlanes * kKBytes;
   static constexpr int kOffBar = kOffK + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers: 2 kStages + 8 words, then the TMEM slot
-  static_assert((2 * kStages + 9) * 8 + 16 <= 256, "attention barrier block");
+  static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers: 2 kStages + 11 words, then the TMEM slot
+  static_assert((2 * kStages + 11) * 8 + 16 <= 256, "attention barrier block");
   // TMEM: S0 [0,128), S1 [128,256), O0 [256, 256 + planes*D), O1 [384, 384 + planes*D).
-  // The probabilities overwrite their scores as packed 16-bit pairs: P_t
-  // plane 0 in columns [128t, 128t + 64), plane 1 in [128t + 64, 128t + 128).
+  // Split form: the probabilities overwrite their scores as packed 16-bit
+  // pairs, P_t plane 0 in columns [128t, 128t + 64), plane 1 in [128t + 64,
+  // 128t + 128).  16-bit form (one plane, D <= 64): P_t has its own columns
+  // [256 + 128t + 64, 256 + 128t + 128) beside O_t, so the next block's
+  // scores can be computed into S_t while P_t still feeds the PV product.
+  static constexpr bool kSeparateP = !SPLIT;
+  static_assert(SPLIT || D <= 64, "O_t and P_t share a 128-column TMEM region");
   static constexpr int kTmemCols = 512;
   static_assert(kSmemBytes <= 232448, "attention shared memory");
 };
@@ -200,7 +205,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* pv_done = p_ready + 2;          // [2]
   uint64_t* drain = pv_done + 2;
   uint64_t* q_empty = drain + 1;            // the S MMAs of a segment have read Q
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_empty + 1);
+  uint64_t* s_free = q_empty + 1;           // [2] the softmax has read S_t into registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -216,6 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_ready[t], 4);
       mbar_init(&pv_done[t], 1);
+      mbar_init(&s_free[t], 4);
     }
     mbar_init(drain, 1);
     mbar_init(q_empty, 1);
@@ -302,6 +309,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       while (ok && sched_next(p, sc, g)) {
       ok = mbar_wait(q_full, seg & 1, abort_flag, status);
+      if constexpr (Cfg::kSeparateP) {
+        // Per key block j: S_t(j) as soon as the softmax has read S_t(j - 1)
+        // and K_j has landed, then PV_t(j - 1) when P_t(j - 1) is ready; the
+        // score product of the next block runs under the softmax of this one.
+        for (int j = 0; ok && j <= g.nblocks; ++j) {
+          const long long cur = blk + j;
+          const int st = static_cast<int>(cur % Cfg::kStages);
+          const int pst = static_cast<int>((cur + Cfg::kStages - 1) % Cfg::kStages);  // stage of block j - 1
+          if (j < g.nblocks) {
+            if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(cur / Cfg::kStages) & 1u, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            for (int t = 0; t < 2 && ok; ++t) {
+              // S_t was last read by the softmax of the previous block (of this or an earlier segment)
+              if (cur > 0 && !mbar_wait(&s_free[t], static_cast<uint32_t>(cur - 1) & 1u, abort_flag, status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t q_addr = smem_u32(smem + t * kPl * Cfg::kQBytes);
+              const uint32_t k_addr = smem_u32(smem + Cfg::kOffK + st * Cfg::kStageBytes);
+#pragma unroll
+              for (int k = 0; k < D / 16; ++k) {
+                const uint64_t ad = make_smem_desc(q_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+                const uint64_t bd = make_smem_desc(k_addr + k * 32, 16, Cfg::kSbo, Cfg::kLayout);
+                umma_ss(tmem + t * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+              }
+              umma_commit(&s_full[t]);
+            }
+          }
+          for (int t = 0; t < 2 && ok && j > 0; ++t) {
+            // P_t(j-1) is in its own columns: O_t += P_t V_{j-1}.
+            if (!mbar_wait(&p_ready[t], static_cast<uint32_t>(cur - 1) & 1u, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t p_tmem = tmem + 256 + t * 128 + 64;
+            const uint32_t v_addr = smem_u32(smem + Cfg::kOffK + pst * Cfg::kStageBytes + kPl * Cfg::kKBytes);
+            const uint32_t o_acc = tmem + 256 + t * 128;
+#pragma unroll
+            for (int k = 0; k < kBlockN / 16; ++k) {
+              const uint64_t bd = make_smem_desc(v_addr + k * 16 * Cfg::kRowBytes, 16 * Cfg::kRowBytes * 8,
+                                                 Cfg::kSbo, Cfg::kLayout);
+              umma_ts(o_acc, p_tmem + k * 8, bd, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&pv_done[t]);
+            if (t == 1) umma_commit(&kv_empty[pst]);
+          }
+        }
+      } else
       for (int j = 0; ok && j <= g.nblocks; ++j) {
         const long long cur = blk + j;  // this block's position in the K/V ring and the tile barriers
         const int st = static_cast<int>(cur % Cfg::kStages);
@@ -379,6 +438,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tmem_s = tmem + t * 128 + lane_base;
     const uint32_t tmem_o = tmem + 256 + t * 128 + lane_base;
+    // where the packed probabilities go: their own columns, or over the scores
+    const uint32_t tmem_p = Cfg::kSeparateP ? tmem_o + 64 : tmem_s;
     const float c = p.scale_log2;
     AttnSched sc = sched_begin(p);
     AttnSeg g;
@@ -403,6 +464,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(tmem_s + c0, chunk);
       }
       tmem_wait_ld();
+      if constexpr (Cfg::kSeparateP) {
+        // the scores are in registers: S_t may take the next block's product
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+      }
       const bool full = valid == kBlockN;
       if (!full) {
         // keys past the end never count: -inf scores give zero probability
@@ -479,7 +546,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         // Keys c0..c0+31 of this row: 16 packed pairs over its scores (all
         // of which are already in registers).
-        tmem_st16(tmem_s + (c0 >> 1), packed);
+        tmem_st16(tmem_p + (c0 >> 1), packed);
         if constexpr (SPLIT) tmem_st16(tmem_s + 64 + (c0 >> 1), packed_lo);
       }
       {

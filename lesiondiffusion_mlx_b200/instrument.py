@@ -32,6 +32,7 @@ class _Record:
     flops: float
     start: torch.cuda.Event
     end: torch.cuda.Event
+    label: str = ""
 
 
 @dataclass
@@ -39,6 +40,7 @@ class _ClockRecord:
     kind: str
     flops: float
     slot: int
+    label: str = ""
 
 
 @dataclass
@@ -49,7 +51,7 @@ class KernelTimer:
     clock_records: list[_ClockRecord] = field(default_factory=list)
     _table: torch.Tensor | None = None
 
-    def clock_pointer(self, kind: str, flops: float, device: torch.device) -> int:
+    def clock_pointer(self, kind: str, flops: float, device: torch.device, label: str = "") -> int:
         """Address of a fresh (start, end) slot of the device clock table."""
         if self._table is None:
             self._table = torch.zeros((self.capacity, 2), dtype=torch.int64, device=device)
@@ -57,7 +59,7 @@ class KernelTimer:
         slot = len(self.clock_records)
         if slot >= self.capacity:
             raise RuntimeError("device clock table is full")
-        self.clock_records.append(_ClockRecord(kind, flops, slot))
+        self.clock_records.append(_ClockRecord(kind, flops, slot, label))
         return self._table[slot].data_ptr()
 
     def arm(self, device: torch.device) -> None:
@@ -82,6 +84,16 @@ class KernelTimer:
         finally:
             end.record()
             self.records.append(_Record(kind, flops, start, end))
+
+    def launches(self) -> list[tuple[str, str, float, float]]:
+        """(kind, label, FLOPs, milliseconds) of every recorded launch of the last replay, in order."""
+        out = [(r.kind, r.label, r.flops, r.start.elapsed_time(r.end)) for r in self.records]
+        if self.clock_records:
+            table = self._table.cpu()
+            for r in self.clock_records:
+                start, end = (int(v) for v in table[r.slot])
+                out.append((r.kind, r.label, r.flops, max(0, end - start) / 1e6))
+        return out
 
     def summary(self) -> dict[str, dict[str, float]]:
         """Per kind: launches, total milliseconds, FLOPs (of the last replay)."""
@@ -118,12 +130,12 @@ def timing(timer: KernelTimer):
         _ACTIVE = previous
 
 
-def device_clock(kind: str, flops: float, device: torch.device) -> int | None:
+def device_clock(kind: str, flops: float, device: torch.device, label: str = "") -> int | None:
     """Clock-slot address for a launch that records its own device clock, or None."""
     timer = _ACTIVE
     if timer is None or not timer.device_clock:
         return None
-    return timer.clock_pointer(kind, flops, device)
+    return timer.clock_pointer(kind, flops, device, label)
 
 
 @contextlib.contextmanager

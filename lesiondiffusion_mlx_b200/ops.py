@@ -211,7 +211,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
     _lib.call("ldb_flash_attention_workspace_size", batch, lq, lk, heads, width // heads, ctypes.byref(ws_bytes))
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=q.device) if ws_bytes.value else None
     flops = 4.0 * batch * lq * lk * width
-    clock = instrument.device_clock("attention", flops, q.device)
+    clock = instrument.device_clock("attention", flops, q.device, f"B{batch} {lq}x{lk} h{heads}x{width // heads}")
     with instrument.maybe_time("attention", flops, device_clocked=clock is not None):
         _lib.call(
             "ldb_flash_attention_timed", _stream(q), q.data_ptr(), int(q.stride(1)), k.data_ptr(), v.data_ptr(),
