@@ -11,8 +11,9 @@ steps), then the config-4 decoder turns the final latent (the 7 denoised
 channels plus the mask channel, 8 channels as the decoder expects) into a
 1 x 128 x 160 x 160 HU volume.  Random-init weights (UNet seed 100, decoder
 seed 200), seeded inputs; the known latent is smoothed N(0, 1) (seed 300)
-and the mask the 8 x 8 x 5 box of the config-3 inputs.  The whole run is
-timed with CUDA events, max over ranks.
+and the mask the 8 x 8 x 5 box of the config-3 inputs.  The schedule is the
+real LINet ``alphas_cumprod`` (f16).  The whole run is timed with CUDA
+events, max over ranks.
 """
 
 from __future__ import annotations
@@ -21,6 +22,7 @@ import argparse
 import datetime
 import json
 import os
+from pathlib import Path
 
 import numpy as np
 import torch
@@ -30,10 +32,14 @@ from .networks import LdmUnetB200, VqDecoderB200
 from .sampling import DdimSampler, Dpmpp2mSampler, PreparedSampler
 
 
+GOLDEN = Path(__file__).resolve().parents[1] / "tests" / "golden" / "reference_fixtures.npz"
+
+
 def _alphas() -> np.ndarray:
-    """The LINet-style scaled-linear schedule (1000 steps) rounded to f16."""
-    betas = np.linspace(0.00085 ** 0.5, 0.012 ** 0.5, 1000, dtype=np.float64) ** 2
-    return np.cumprod(1.0 - betas).astype(np.float16)
+    """The real LINet ``alphas_cumprod`` (1000 entries, f16) from the reference's
+    DPM++ recording, the schedule config 5 names."""
+    with np.load(GOLDEN, allow_pickle=False) as archive:
+        return archive["dpmpp_2m/linet_4.alphas_cumprod"]
 
 
 def main() -> None:
