@@ -2,6 +2,7 @@
 ``ncu`` captures summarised under ``profiles/``).
 
     python -m lesiondiffusion_mlx_b200.kernel_cases [conv|attention|norm|all] [--case NAME] [--iters N]
+    python -m lesiondiffusion_mlx_b200.kernel_cases step [--eager N]   # config-3 step launch table
 
 Each case runs on seeded random inputs and prints one JSON line per case with
 the CUDA-event time per launch (back-to-back launches replayed from a CUDA
@@ -128,13 +129,85 @@ def norm_case(iters: int) -> list[dict]:
     return out
 
 
+def _config3_step():
+    """The config-3 denoise step of ``bench.py``: UNet (seed 100) + fused DDIM update, prepared."""
+    from pathlib import Path
+
+    import numpy as np
+
+    from . import workloads
+    from .networks import LdmUnetB200
+    from .sampling import DdimSampler, PreparedSampler
+
+    golden = Path(__file__).resolve().parents[1] / "tests" / "golden" / "reference_fixtures.npz"
+    with np.load(golden, allow_pickle=False) as archive:
+        alphas = archive["dpmpp_2m/linet_4.alphas_cumprod"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = workloads.CONFIG3
+    raw = workloads.unet_weights(cfg, 8, 8, 768, seed=100)
+    unet = LdmUnetB200({k: torch.from_numpy(v).half() for k, v in raw.items()}, cfg, device=dev)
+    inp = workloads.config3_inputs(seed=101)
+    cache = unet.prepare_context(torch.from_numpy(inp["context"]).to(dev))
+    image = torch.from_numpy(workloads.source_latent((1, 7, 32, 40, 40), seed=300)).permute(0, 2, 3, 4, 1)
+    prepared = PreparedSampler(DdimSampler(alphas, 200), unet, cache, image.to(dev),
+                               torch.from_numpy(inp["mask"][:, 0]).to(dev), graph=False)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    prepared.begin(torch.randn(prepared.state.x.shape, generator=g, device=dev),
+                   torch.randn(prepared.state.noise.shape, generator=g, device=dev))
+    return prepared
+
+
+def step_case(eager: int, iters: int) -> list[dict]:
+    """``eager`` > 0: that many eager config-3 steps (every launch separate, for
+    ncu).  Otherwise: the step as a CUDA graph, its mean time over ``iters``
+    replays, and one row per launch kind and shape from the device-clock
+    timer (conv and attention launches time themselves; the rest have event
+    pairs, which add gaps)."""
+    from . import instrument
+
+    prepared = _config3_step()
+    if eager > 0:
+        for _ in range(eager):
+            prepared._step()
+        torch.cuda.synchronize()
+        return [{"kernel": "config3_step", "eager_steps": eager}]
+    timer = instrument.KernelTimer(device_clock=True)
+    timer.arm(prepared.state.x.device)
+    prepared._step()
+    torch.cuda.synchronize()
+    timed = torch.cuda.CUDAGraph()
+    with instrument.timing(timer), torch.cuda.graph(timed):
+        prepared._step()
+    ms = _time(prepared._step, iters)
+    for _ in range(3):
+        timer.reset()
+        timed.replay()
+    torch.cuda.synchronize()
+    rows: dict[tuple[str, str], list[float]] = {}
+    for kind, label, flops, t in timer.launches():
+        r = rows.setdefault((kind, label), [0, 0.0, 0.0])
+        r[0] += 1
+        r[1] += t
+        r[2] += flops
+    out = [{"kernel": "config3_step", "ms_per_step": ms}]
+    for (kind, label), (n, t, flops) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+        out.append({"kernel": kind, "shape": label, "launches": n, "ms": t, "us_per_launch": 1e3 * t / n,
+                    "tflops": flops / t / 1e9 if t and flops else None})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", nargs="?", default="all", choices=("conv", "attention", "norm", "all"))
+    ap.add_argument("what", nargs="?", default="all", choices=("conv", "attention", "norm", "step", "all"))
     ap.add_argument("--case", default=None)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--stats", action="store_true", help="conv cases also accumulate GroupNorm statistics")
+    ap.add_argument("--eager", type=int, default=0, help="step: run this many eager steps (for ncu) and exit")
     a = ap.parse_args()
+    if a.what == "step":
+        for r in step_case(a.eager, a.iters):
+            print(json.dumps(r), flush=True)
+        return
     if a.what in ("conv", "all"):
         for name in ([a.case] if a.case else CONV_CASES):
             print(json.dumps(conv_case(name, a.iters, stats=a.stats)), flush=True)
