@@ -64,11 +64,27 @@ __device__ __forceinline__ TileCoord decode_tile(const ConvParams& p, int t) {
   return c;
 }
 
+// Tile index (as decode_tile reads it) that CTA `rank` of a pair computes for
+// work unit u = (pair q, column tile, K range).  A pair shares its weight
+// operand, so its two row tiles are two spatial bricks of the same output
+// parity (the folded upsampling conv has one weight set per parity): pair q
+// = (spatial pair qs, parity) takes bricks 2 qs and 2 qs + 1.  Past the last
+// brick the index decodes to batch index p.batch (a placeholder).
+__device__ __forceinline__ int pair_tile(const ConvParams& p, int u, int rank) {
+  const int ks = u % p.k_splits;
+  const int r = u / p.k_splits;
+  const int nt = r % p.n_tiles;
+  const int q = r / p.n_tiles;
+  const int par = q % p.parities;
+  const int brick = 2 * (q / p.parities) + rank;
+  return ((brick * p.parities + par) * p.n_tiles + nt) * p.k_splits + ks;
+}
+
 // Output voxel (linear NDHW index) of GEMM row `r` of a tile, or -1 when
 // the row falls outside the brick or the volume.
 __device__ __forceinline__ long long row_voxel(const ConvParams& p, const TileCoord& c, int r) {
   const int brick = p.bw * p.bh * p.bd;
-  if (r >= brick) return -1;
+  if (r >= brick || c.b >= p.batch) return -1;  // b == batch: a pair's placeholder tile
   const int lw = r % p.bw;
   const int lh = (r / p.bw) % p.bh;
   const int ld = r / (p.bw * p.bh);
@@ -176,7 +192,7 @@ __device__ __forceinline__ void store_outputs(const ConvParams& p, int b, long l
 
 // TRANS: channel-major tile (activation rows are the MMA's N operand, up to
 // 256 voxels; the weight tile is the M = 128 operand).
-template <int KC, int BN, bool EXACT, bool TRANS = false>
+template <int KC, int BN, bool EXACT, bool TRANS = false, bool PAIR = false>
 struct ConvCfg {
   static constexpr int kSwizzleBytes = KC * 2;  // one K block row = 32/64/128 B
   static constexpr uint32_t kLayout = KC == 64 ? kSwizzle128 : (KC == 32 ? kSwizzle64 : kSwizzle32);
@@ -184,7 +200,9 @@ struct ConvCfg {
   static constexpr int kPlanes = EXACT ? 2 : 1;
   static constexpr int kRowsA = TRANS ? 192 : kTileM;  // activation rows per stage (bricks of <= 3 planes)
   static constexpr int kABytes = kRowsA * KC * 2;
-  static constexpr int kBBytesRaw = BN * KC * 2;
+  // PAIR: this CTA stages half of the BN weight rows (the peer the other half).
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;
+  static constexpr int kBBytesRaw = kBRows * KC * 2;
   static constexpr int kBBytes = ((kBBytesRaw + 1023) / 1024) * 1024;
   static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
   // Epilogue staging: output + 2 residual buffers of 128 rows x 128 bytes;
@@ -193,6 +211,9 @@ struct ConvCfg {
   // its ring holds a fourth stage: with ~1.2 us per TMA round trip the
   // bytes in flight bound that pipeline.
   static constexpr int kEpiBufBytes = kTileM * 128;
+  // (Paired tiles keep two: their grids are mostly one work unit per CTA, so
+  // the epilogue is the CTA's tail, not hidden behind a next tile's main loop;
+  // one buffer and a fifth ring stage measured 4-8 % slower.)
   static constexpr int kOutBufs = TRANS ? 1 : 2;
   static constexpr int kEpiBytes = (kOutBufs + 2) * kEpiBufBytes;
   // Per-CTA GroupNorm statistics accumulator: [BN][2] FP32 shifted sums
@@ -217,13 +238,14 @@ struct ConvCfg {
   static constexpr int kOutBytes = EXACT ? 4 : 2;
   static constexpr int kOutChunk = (128 / kOutBytes) < BN ? (128 / kOutBytes) : BN;
   static constexpr int kPartChunk = 32 < BN ? 32 : BN;  // split-K partials are f32
-  static constexpr uint32_t kIdesc = make_idesc_f16(kTileM, BN, 0, 0, 0);
+  static constexpr uint32_t kIdesc = make_idesc_f16(PAIR ? 2 * kTileM : kTileM, BN, 0, 0, 0);
   // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, res_full[2]
   static constexpr int kBarrierBytes = (2 * kStages + 7) * 8;
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kEpiBytes + 1024 /*align slack*/ + kBarrierBytes + 64 + BN * 4 + kStatsBytes;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
   static_assert(!TRANS || (BN == 128 && !EXACT), "channel-major tiles are f16 with 128 channel rows");
+  static_assert(!PAIR || (BN == 256 && !EXACT && !TRANS), "CTA pairs run the f16 voxel-major 256-column tile");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
 };
 
@@ -357,7 +379,10 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
   const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
   const int omap = p.mode == kConvUp2 ? c.par : 0;
   const int n0 = c.nt * BN;
-  const bool has_res = !SPLIT && p.residual != nullptr;
+  // A pair's placeholder tile (batch index past the end) drains its
+  // accumulator like any tile but reads and writes nothing in global memory.
+  const bool real = c.b < p.batch;
+  const bool has_res = !SPLIT && p.residual != nullptr && real;
   const uint32_t res_bytes = kRowBytes * static_cast<uint32_t>(p.bw * p.bh * p.bd);
   uint8_t* const res_base = st.epi + Cfg::kOutBufs * Cfg::kEpiBufBytes;  // residual buffer rb at res_base + rb * kEpiBufBytes
   if (has_res && st.leader) {
@@ -389,7 +414,7 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
     for (int j = et; j < BN; j += 128) {
       const int col = n0 + j;
       float add = 0.f;
-      if (col < p.cout) {
+      if (col < p.cout && real) {
         if (p.bias) add = p.bias[col];
         if (p.shift) add += p.shift[static_cast<long long>(c.b) * p.cout + col];
       }
@@ -404,9 +429,14 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
   const uint32_t rowoff = static_cast<uint32_t>(st.row) * kRowBytes;
 #pragma unroll 1
   for (int q = 0; q < kChunks; ++q) {
-    uint8_t* ob = st.epi + (st.oq & 1) * Cfg::kEpiBufBytes;
+    uint8_t* ob = st.epi + (Cfg::kOutBufs == 2 ? (st.oq & 1) * Cfg::kEpiBufBytes : 0);
     if (st.leader) {
-      bulk_wait_group_read<1>();  // the store issued two chunks ago has read this buffer
+      // the store issued kOutBufs chunks ago has read this buffer
+      if constexpr (Cfg::kOutBufs == 2) {
+        bulk_wait_group_read<1>();
+      } else {
+        bulk_wait_group_read<0>();
+      }
       if (has_res && q + 1 < kChunks) {
         const int rb = (st.rq + 1) & 1;
         mbar_arrive_expect_tx(&st.res_full[rb], res_bytes);
@@ -509,7 +539,7 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
     }
     fence_proxy_async_smem();
     named_barrier(1, 128);
-    if (st.leader) {
+    if (st.leader && real) {
       if constexpr (SPLIT) {
         const int prow = (c.ks * (p.num_tiles / p.k_splits) + c.out_tile) * kTileM;
         tma_store_2d(&maps.part, ob, c0, prow);
@@ -675,11 +705,11 @@ __device__ __forceinline__ bool epilogue_tile_trans(const ConvParams& p, const C
   return ok;
 }
 
-template <int KC, int BN, bool EXACT, bool TRANS>
-__global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
+template <int KC, int BN, bool EXACT, bool TRANS, bool PAIR>
+__global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS, PAIR>::kThreads, 1)
     conv3d_tc_kernel(const __grid_constant__ ConvMaps maps, const __grid_constant__ CUtensorMap wmap,
                      const ConvParams p, unsigned int* status) {
-  using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
+  using Cfg = ConvCfg<KC, BN, EXACT, TRANS, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + Cfg::kStages * Cfg::kStageBytes;  // out[kOutBufs] | res[2], 1024-aligned
@@ -697,6 +727,14 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  // Work: without pairs CTA i takes tiles i, i + grid, ...; with pairs the
+  // cluster (two CTAs) takes units j, j + grid / 2, ... and CTA `rank` of it
+  // computes the unit's row tile 2q + rank.
+  const int rank = PAIR ? static_cast<int>(cluster_ctarank()) : 0;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int units = PAIR ? p.num_units : p.num_tiles;
+  auto tile_of = [&](int u) { return PAIR ? pair_tile(p, u, rank) : u; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
@@ -705,7 +743,8 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      // with pairs the leader's accumulator is free once both CTAs' epilogues have read it
+      mbar_init(&acc_empty[a], PAIR ? 8 : 4);
     }
     mbar_init(drain, 1);
     mbar_init(&res_full[0], 1);
@@ -729,11 +768,17 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or load
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Programmatic dependent launch: the next kernel may be scheduled at once;
@@ -764,13 +809,14 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
       uint32_t armed_mask = 0, armed_parity = 0;
       bool waited = false;
       int jt = 0;  // sequence index of the current tile's first K block, mod P
-      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
-        const TileCoord c = decode_tile(p, t);
+      for (int u = unit0; u < units && !*abort_flag; u += unit_step) {
+        const TileCoord c = decode_tile(p, tile_of(u));
         const int kb0 = c.ks * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         const int w0 = c.tw * p.bw, h0 = c.th * p.bh, d0 = c.td * p.bd;
         const int pd = c.par >> 2, ph = (c.par >> 1) & 1, pw = c.par & 1;
-        const int brow = c.par * p.wrows_per_parity + c.nt * BN;
+        // (a pair's CTA r stages weight rows [128 r, 128 r + 128) of the column tile)
+        const int brow = c.par * p.wrows_per_parity + c.nt * BN + rank * Cfg::kBRows;
         int kb = kb0 + (pid - jt + P) % P;  // this producer's first K block of the tile
         jt = (jt + kb1 - kb0) % P;
         if (kb >= kb1) continue;
@@ -801,9 +847,12 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
           }
           uint8_t* sa = smem + stage * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kPlanes * Cfg::kABytes;
-          mbar_arrive_expect_tx(&full[stage], tx_bytes);
-          armed_mask |= 1u << stage;
-          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          if (!PAIR || rank == 0) {
+            // a pair's leader counts both CTAs' bytes: the loads of both complete on its barrier
+            mbar_arrive_expect_tx(&full[stage], PAIR ? 2 * tx_bytes : tx_bytes);
+            armed_mask |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
           int map = 0, x = w0, y = h0, z = zb;
           if (p.mode == kConv3x3x3) {
             x += kw - 1;
@@ -836,8 +885,14 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
             if (p.clock) atomicMin(p.clock, static_cast<unsigned long long>(globaltimer_ns()));
           }
           const int chn = chunk * KC;
-          tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
-          tma_load_2d(sb, &wmap, &full[stage], kb * KC, brow);
+          if constexpr (PAIR) {
+            const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_5d_pair(sa, &maps.a[map], bar, chn, x, y, z, c.b);
+            tma_load_2d_pair(sb, &wmap, bar, kb * KC, brow);
+          } else {
+            tma_load_5d(sa, &maps.a[map], &full[stage], chn, x, y, z, c.b);
+            tma_load_2d(sb, &wmap, &full[stage], kb * KC, brow);
+          }
           if (EXACT) {
             tma_load_5d(sa + Cfg::kABytes, &maps.a[map], &full[stage], p.cin_pad + chn, x, y, z, c.b);
             tma_load_2d(sb + Cfg::kBBytes, &wmap, &full[stage], p.taps * p.cin_pad + kb * KC, brow);
@@ -875,7 +930,8 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (with pairs only the leader issues: one M = 256 product per K step)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -883,8 +939,8 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
       uint32_t stage_addr = smem_base;  // shared address of the current stage
       const uint64_t desc_const = make_smem_desc(0, 16, Cfg::kSbo, Cfg::kLayout);
       const uint32_t trans_idesc = TRANS ? make_idesc_f16(128, p.trans_n, 0, 0, 0) : 0u;
-      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++local) {
-        const TileCoord c = decode_tile(p, t);
+      for (int u = unit0; u < units && !*abort_flag; u += unit_step, ++local) {
+        const TileCoord c = decode_tile(p, tile_of(u));
         const int kb0 = c.ks * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         const int acc = local & 1;
@@ -920,6 +976,10 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
               umma_ss(d_hi + (step & 1) * BN, ad, bd, Cfg::kIdesc, step >= 2 ? 1u : 0u);
               continue;
             }
+            if constexpr (PAIR) {
+              umma_ss_pair(d_hi, ad, bd, Cfg::kIdesc, accum);
+              continue;
+            }
             umma_ss(d_hi, ad, bd, Cfg::kIdesc, accum);
             if (EXACT) {
               const uint64_t ad_lo = ad + (Cfg::kABytes >> 4);
@@ -928,7 +988,11 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
               umma_ss(d_lo, ad_lo, bd, Cfg::kIdesc, 1u);
             }
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) {
+            umma_commit_pair(&empty[stage], 3);  // frees the stage in both CTAs
+          } else {
+            umma_commit(&empty[stage]);
+          }
           if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -938,10 +1002,18 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[acc]);
+        if constexpr (PAIR) {
+          umma_commit_pair(&acc_full[acc], 3);  // both CTAs' halves of the accumulator are ready
+        } else {
+          umma_commit(&acc_full[acc]);
+        }
       }
       // All issued MMAs must finish before TMEM is released.
-      umma_commit(drain);
+      if constexpr (PAIR) {
+        umma_commit_pair(drain, 1);
+      } else {
+        umma_commit(drain);
+      }
       volatile int never = 0;
       mbar_wait(drain, 0, &never, status);
     }
@@ -961,8 +1033,8 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
     st.leader = threadIdx.x == 64;
     const bool split = p.k_splits > 1;
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
-      const TileCoord c = decode_tile(p, t);
+    for (int u = unit0; u < units; u += unit_step, ++local) {
+      const TileCoord c = decode_tile(p, tile_of(u));
       const int acc = local & 1;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(st.quarter * 32) << 16) + acc * Cfg::kAccCols;
       bool ok;
@@ -976,7 +1048,13 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
       (void)ok;  // a failed wait already raised the abort flag and the device status
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR) {
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));  // the leader's barrier
+        } else {
+          mbar_arrive(&acc_empty[acc]);
+        }
+      }
     }
     if constexpr (TRANS) {
       if (p.stats) flush_trans_stats(p, st);
@@ -992,9 +1070,17 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS>::kThreads, 1)
 
   __syncwarp();
   __syncthreads();
+  // With pairs: the leader's MMAs read this CTA's shared memory and write its
+  // TMEM, so neither CTA releases either before both have finished (the
+  // leader's MMA thread drained all MMAs before reaching this point).
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
   }
 }
 
@@ -1143,11 +1229,11 @@ void choose_brick(int d, int h, int w, bool pointwise, int* bd, int* bh, int* bw
   *bw = best[2];
 }
 
-template <int KC, int BN, bool EXACT, bool TRANS = false>
+template <int KC, int BN, bool EXACT, bool TRANS = false, bool PAIR = false>
 int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wmap, const ConvParams& p,
                 int grid) {
-  using Cfg = ConvCfg<KC, BN, EXACT, TRANS>;
-  auto kernel = conv3d_tc_kernel<KC, BN, EXACT, TRANS>;
+  using Cfg = ConvCfg<KC, BN, EXACT, TRANS, PAIR>;
+  auto kernel = conv3d_tc_kernel<KC, BN, EXACT, TRANS, PAIR>;
   int smem = Cfg::kSmemBytes;
   // Keep one CTA per SM when the accumulators need more than half of TMEM,
   // so co-resident CTAs never queue on tcgen05.alloc.
@@ -1158,8 +1244,14 @@ int launch_conv(cudaStream_t stream, const ConvMaps& maps, const CUtensorMap& wm
                                          "conv smem attribute");
     if (rc != LDB_OK) return rc;
   }
-  int rc = launch_kernel(kernel, dim3(grid), dim3(Cfg::kThreads), smem, stream, "conv3d launch", maps, wmap, p,
-                         device_status_ptr());
+  int rc;
+  if constexpr (PAIR) {
+    rc = launch_kernel_cluster(kernel, dim3(grid), dim3(Cfg::kThreads), smem, stream, "conv3d (CTA pairs) launch", 2u,
+                               maps, wmap, p, device_status_ptr());
+  } else {
+    rc = launch_kernel(kernel, dim3(grid), dim3(Cfg::kThreads), smem, stream, "conv3d launch", maps, wmap, p,
+                       device_status_ptr());
+  }
   if (rc != LDB_OK) return rc;
   if (p.k_splits > 1) {
     // Many K ranges: one row per thread (more blocks, more loads in flight);
@@ -1184,7 +1276,10 @@ int dispatch_bn(int bn, cudaStream_t stream, const ConvMaps& maps, const CUtenso
     case 64: return launch_conv<KC, 64, EXACT>(stream, maps, wmap, p, grid);
     case 128: return launch_conv<KC, 128, EXACT>(stream, maps, wmap, p, grid);
     case 256:
-      if constexpr (!EXACT) return launch_conv<KC, 256, false>(stream, maps, wmap, p, grid);
+      if constexpr (!EXACT) {
+        if (p.pair) return launch_conv<KC, 256, false, false, true>(stream, maps, wmap, p, grid);
+        return launch_conv<KC, 256, false>(stream, maps, wmap, p, grid);
+      }
       break;
   }
   return fail(LDB_ERR_SHAPE, "no conv kernel for BN=%d", bn);
@@ -1194,6 +1289,15 @@ int dispatch_bn(int bn, cudaStream_t stream, const ConvMaps& maps, const CUtenso
 bool conv_trans_enabled() {
   static const bool enabled = [] {
     const char* v = std::getenv("LDB_CONV_TRANS");
+    return !(v && v[0] == '0');
+  }();
+  return enabled;
+}
+
+// CTA pairs for the 256-column tile are on unless LDB_CONV_PAIR=0 (for comparisons).
+bool conv_pair_enabled() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("LDB_CONV_PAIR");
     return !(v && v[0] == '0');
   }();
   return enabled;
@@ -1307,7 +1411,17 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     p.n_tiles = (cout + bn - 1) / bn;
     p.wrows_per_parity = p.n_tiles * bn;
   }
-  const long long tiles_now = static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
+  const long long bricks = static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w;
+  const long long m_tiles = bricks * p.parities;
+  // CTA pairs for the f16 256-column 3x3x3 tile: each CTA of a pair stages
+  // its 128-voxel brick and half of the 256 weight rows (32 KB per K block
+  // instead of 48), so a stage carries 1.5x the FLOPs per staged byte and the
+  // ring keeps more K blocks in flight.
+  const bool pair = !exact && bn == 256 && taps > 1 && bricks >= 2 && conv_pair_enabled();
+  // pairs of same-parity bricks (see pair_tile)
+  const long long pairs = (bricks + 1) / 2 * p.parities;
+  // CTAs one K range of every output tile needs (a pair's placeholder tile counts)
+  const long long tiles_now = (pair ? 2 * pairs : m_tiles) * p.n_tiles;
   int splits = 1;
   if (taps > 1 && tiles_now < sms && p.kb_total >= 8) {
     splits = static_cast<int>(std::min<long long>(sms / tiles_now, p.kb_total / 4));
@@ -1319,7 +1433,10 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   }
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
-  p.num_tiles = static_cast<int>(tiles_now * p.k_splits);
+  p.num_tiles = static_cast<int>(m_tiles * p.n_tiles * p.k_splits);
+  p.pair = pair ? 1 : 0;
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.num_units = pair ? static_cast<int>(pairs * p.n_tiles * p.k_splits) : 0;
   p.cout = cout;
   p.out_ld = d->out_ld;
   p.res_ld = d->res_ld;
@@ -1360,6 +1477,7 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
       }
     }
     p.trans = 1;
+    p.pair = 0;
     p.bd = best_bd;
     p.bh = 8;
     p.bw = 8;
@@ -1372,7 +1490,8 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
     p.num_tiles = static_cast<int>(static_cast<long long>(B) * p.tiles_d * th * tw * p.parities);
     plan->bn = 128;
   }
-  plan->grid = static_cast<int>(std::min<long long>(p.num_tiles, sms));
+  plan->grid = p.pair ? 2 * static_cast<int>(std::min<long long>(p.num_units, sms / 2))
+                      : static_cast<int>(std::min<long long>(p.num_tiles, sms));
   plan->workspace = p.k_splits > 1 ? static_cast<size_t>(p.num_tiles) * kTileM * bn * sizeof(float) : 0;
   return LDB_OK;
 }
@@ -1518,7 +1637,8 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
   const uint64_t wrows = static_cast<uint64_t>(p.parities) * p.wrows_per_parity;
   const uint64_t wdims[2] = {ktotal, wrows};
   const uint64_t wstrides[1] = {ktotal * esz};
-  const uint32_t wbox[2] = {static_cast<uint32_t>(plan.kc), static_cast<uint32_t>(plan.bn)};
+  // (a pair's CTA stages half of the column tile's weight rows)
+  const uint32_t wbox[2] = {static_cast<uint32_t>(plan.kc), static_cast<uint32_t>(p.pair ? plan.bn / 2 : plan.bn)};
   rc = encode_tiled_f16(&wmap, w_packed, 2, wdims, wstrides, wbox, plan.kc * 2);
   if (rc != LDB_OK) return rc;
 

@@ -41,6 +41,15 @@ struct ConvParams {
   int in_zoff;           // depth index of output slice 0's centre tap in x (the depth halo)
   int wrows_per_parity;  // packed weight rows per parity (Cout padded to BN)
   int num_tiles;         // batch * tiles * parities * n_tiles * k_splits
+  // CTA pairs (cta_group::2, voxel-major 256-column tile): two spatial
+  // bricks of the same output parity form a pair, computed as one M = 256
+  // product by the two CTAs of a cluster; a pair's second brick past the last
+  // one is a placeholder whose loads read zeros and whose results are
+  // dropped.  Work units are (pair, column tile, K range).  pair = 0: one CTA
+  // per tile.
+  int pair;
+  int m_tiles;    // batch * tiles * parities
+  int num_units;  // ceil(bricks / 2) * parities * n_tiles * k_splits when pair
   // Epilogue: out = act((acc + bias + shift[b]) * scale + residual), stored as
   // f16 or f32 in NDHWC with channel stride out_ld; with k_splits > 1 raw f32
   // partial tiles go to `partials` and the reduction kernel applies it.

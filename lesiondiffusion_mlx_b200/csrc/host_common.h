@@ -56,6 +56,29 @@ int launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...), what);
 }
 
+// launch_kernel for a kernel whose CTAs run in clusters of `cluster_x` along
+// x (gridDim.x a multiple of it).
+template <typename... Params, typename... Args>
+int launch_kernel_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          const char* what, unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  count_launch();
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...), what);
+}
+
 // Raise a kernel's dynamic shared-memory limit once per device (the
 // attribute is per device; setting it again inside a graph capture is
 // avoided).  `flags` is the caller's per-kernel bitset of configured devices.

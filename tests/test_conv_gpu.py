@@ -125,6 +125,56 @@ def test_upsample_conv_matches_conv_of_nearest_upsampling(cuda_device):
     assert np.all(error <= half_spacing(expected) + (ACCUMULATION_EPS + OPERAND_ROUNDING) * mag)
 
 
+@pytest.mark.parametrize(
+    ("shape", "out_channels", "kind"),
+    [
+        ((1, 256, 5, 7, 6), 256, "up"),  # folded upsampling: a pair holds two bricks of one output parity
+        ((1, 256, 8, 10, 10), 512, "conv"),  # two 256-column tiles, split over K
+        ((2, 256, 6, 9, 5), 256, "s2"),  # stride 2, batch 2
+        ((1, 128, 3, 9, 14), 256, "conv"),  # three bricks: the second pair's second brick is a placeholder
+    ],
+)
+def test_paired_cta_tiles(cuda_device, shape, out_channels, kind):
+    """256-column f16 3x3x3 convs run as CTA pairs (one M = 256 product of two
+    bricks per K step, each CTA staging half of the weight rows): outputs with
+    per-batch shift and residual within the analytic bound, and the GroupNorm
+    statistics the epilogue adds equal to the sums of the stored output."""
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_upsample_weight, pack_weight
+
+    x, w, b = f16_case(shape, out_channels, 3, seed=sum(shape) + out_channels)
+    batch = shape[0]
+    stride = 2 if kind == "s2" else 1
+    if kind == "up":
+        out_grid = tuple(2 * n for n in shape[2:])
+        packed = pack_upsample_weight(w.to(cuda_device))
+    else:
+        out_grid = tuple((n - 1) // stride + 1 for n in shape[2:])
+        packed = pack_weight(w.to(cuda_device), stride=stride)
+    rng = np.random.default_rng(7)
+    shift = torch.from_numpy(rng.normal(size=(batch, out_channels)).astype(np.float32) * 0.1)
+    residual = torch.from_numpy(rng.normal(size=(batch, out_channels, *out_grid)).astype(np.float16))
+    stats = torch.zeros((batch, out_channels, 2), dtype=torch.float64, device=cuda_device)
+    out = conv3d_ndhwc(to_ndhwc(x.to(cuda_device)), packed, b.to(cuda_device).float(), stride=stride,
+                       shift=shift.to(cuda_device), residual=to_ndhwc(residual.to(cuda_device)).contiguous(),
+                       stats=stats)
+    torch.cuda.synchronize()
+    actual = out.permute(0, 4, 1, 2, 3).double().cpu().numpy()
+    xin = x.double()
+    rounding = ACCUMULATION_EPS
+    if kind == "up":
+        xin = xin.repeat_interleave(2, 2).repeat_interleave(2, 3).repeat_interleave(2, 4)
+        rounding += OPERAND_ROUNDING
+    products, mag = reference(xin, w.double(), b.double(), stride, 1)
+    expected = products + shift.double().numpy()[:, :, None, None, None] + residual.double().numpy()
+    assert actual.shape == expected.shape
+    error = np.abs(actual - expected)
+    bound = half_spacing(expected) + rounding * mag
+    assert np.all(error <= bound), f"max excess {(error - bound).max()}"
+    sums = actual.reshape(batch, out_channels, -1)
+    want = np.stack([sums.sum(-1), (sums * sums).sum(-1)], axis=-1)
+    np.testing.assert_allclose(stats.cpu().numpy(), want, rtol=1e-5, atol=1e-3)
+
+
 @pytest.mark.parametrize("shape,out_channels", [((2, 48, 3, 5, 7), 40), ((1, 256, 2, 4, 100), 512)])
 def test_pointwise_conv_and_gelu(cuda_device, shape, out_channels):
     from lesiondiffusion_mlx_b200 import _lib
