@@ -69,6 +69,12 @@ LDB_API int ldb_version(void);
  * graph) in this process, for launch accounting in benchmarks. */
 LDB_API unsigned long long ldb_launch_count(void);
 
+/* Zero `bytes` bytes of device memory at ptr, ordered on the stream (a
+ * memset; in a captured CUDA graph a memset node, not a kernel).  The
+ * networks clear their GroupNorm statistics arena (the FP64 sums that
+ * ldb_conv3d_fwd_gn_stats adds to) with it before each forward. */
+LDB_API int ldb_clear_async(ldb_stream_t stream, void* ptr, size_t bytes);
+
 /* Message describing the last failure on the calling thread. */
 LDB_API const char* ldb_last_error(void);
 
@@ -338,6 +344,13 @@ LDB_API int ldb_resize_nearest(ldb_stream_t stream, const void* x, int batch, in
 /* Inverse CT map to HU of channel 0 of n voxels (piecewise_ct(inverse=True),
  * mlx_pipeline.py:72-96). */
 LDB_API int ldb_hu_map(ldb_stream_t stream, const void* x, int dtype, int x_ld, long long n, float* out);
+
+/* Forward CT map of n f32 HU values to the normalized range (piecewise_ct,
+ * mlx_pipeline.py:72-96, inverse=False): knots (-1000, -200, 200, 1000) ->
+ * (0, 0.2, 0.8, 1) with clipping, FP32 arithmetic, one rounding to out_dtype
+ * (LDB_F16 for the VQ encoder input, medmlx.py:1289-1291); element i is
+ * written at out + i * out_ld. */
+LDB_API int ldb_ct_normalize(ldb_stream_t stream, const float* hu, long long n, void* out, int out_dtype, int out_ld);
 
 /* -------------------------------------------------------------------------
  * Output-region compositing of a generated CT into the input CT

@@ -66,6 +66,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_version": [],
     "ldb_launch_count": [],
     "ldb_last_error": [],
+    "ldb_clear_async": [_P, _P, _SZ],
     "ldb_device_status": [ctypes.POINTER(ctypes.c_uint), _I],
     "ldb_conv3d_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_SZ)],
     "ldb_conv3d_weight_rows": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_I), ctypes.POINTER(_I)],
@@ -96,6 +97,7 @@ SIGNATURES: dict[str, list] = {
     "ldb_lesion_extent": [_P, _P, _I, _I, _I, _P],
     "ldb_apply_lesion_change": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P],
     "ldb_hu_map": [_P, _P, _I, _I, ctypes.c_longlong, _P],
+    "ldb_ct_normalize": [_P, _P, ctypes.c_longlong, _P, _I, _I],
 }
 _RESTYPES = {"ldb_last_error": ctypes.c_char_p, "ldb_launch_count": ctypes.c_ulonglong}
 

@@ -187,8 +187,10 @@ def resize_nearest(x: torch.Tensor, shape: tuple[int, ...], *, mx=None) -> torch
 
 
 def piecewise_ct(array: torch.Tensor, mx=None, *, inverse: bool = False) -> torch.Tensor:
-    """Normalized -> HU map (``inverse=True``, mlx_pipeline.py:72-96) on the device."""
-    if not inverse:
-        raise NotImplementedError("only the decoder-side inverse map is on the B200 path")
-    flat = array.reshape(1, -1, 1)
-    return ops.hu_map(flat).reshape(array.shape)
+    """Four-knot CT map on the device (mlx_pipeline.py:72-96): HU -> normalized,
+    or normalized -> HU with ``inverse=True``; float32 result of ``array``'s shape."""
+    if inverse:
+        flat = array.reshape(1, -1, 1)
+        return ops.hu_map(flat).reshape(array.shape)
+    flat = array.to(torch.float32).contiguous().reshape(1, -1)
+    return ops.ct_normalize(flat, out_dtype=torch.float32, pad_to=1).reshape(array.shape)

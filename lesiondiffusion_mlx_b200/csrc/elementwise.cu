@@ -355,6 +355,32 @@ __global__ void hu_map_kernel(const void* x, int x_f32, int x_ld, long long n, f
   out[i] = r;
 }
 
+// HU -> normalized with knots (-1000, -200, 200, 1000) -> (0, .2, .8, 1) and
+// clipping (mlx_pipeline.py:72-96, inverse=False): FP32 arithmetic, one
+// rounding to the output dtype (f16 for the encoder input, medmlx.py:1289-1291).
+// Output element i at i * out_ld (channel 0 of an NDHWC buffer).
+__global__ void ct_normalize_kernel(const float* hu, long long n, void* out, int out_f32, int out_ld) {
+  pdl_begin();
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float a = hu[i];
+  const float kin[4] = {-1000.0f, -200.0f, 200.0f, 1000.0f};
+  const float kout[4] = {0.0f, 0.2f, 0.8f, 1.0f};
+  float r = kout[0];
+#pragma unroll
+  for (int s = 0; s < 3; ++s) {
+    const float slope = static_cast<float>((static_cast<double>(kout[s + 1]) - kout[s]) /
+                                           (static_cast<double>(kin[s + 1]) - kin[s]));
+    if (a >= kin[s] && a < kin[s + 1]) r = __fadd_rn(__fmul_rn(slope, __fsub_rn(a, kin[s])), kout[s]);
+  }
+  if (a >= kin[3]) r = kout[3];
+  if (out_f32) {
+    static_cast<float*>(out)[i * out_ld] = r;
+  } else {
+    static_cast<__half*>(out)[i * out_ld] = __float2half_rn(r);
+  }
+}
+
 __global__ void step_advance_kernel(int* step) {
   pdl_begin();
   *step += 1;
@@ -482,6 +508,16 @@ int ldb_hu_map(cudaStream_t stream, const void* x, int dtype, int x_ld, long lon
   const int threads = 256;
   return launch_kernel(hu_map_kernel, dim3(static_cast<unsigned>((n + threads - 1) / threads)), dim3(threads), 0,
                        stream, "hu_map launch", x, int(dtype == LDB_F32), x_ld, n, out);
+}
+
+int ldb_ct_normalize(cudaStream_t stream, const float* hu, long long n, void* out, int out_dtype, int out_ld) {
+  using namespace ldb;
+  if (!hu || !out || n <= 0) return fail(LDB_ERR_INVALID, "ct_normalize: bad arguments");
+  if (out_dtype != LDB_F16 && out_dtype != LDB_F32) return fail(LDB_ERR_INVALID, "ct_normalize: out dtype f16 or f32");
+  if (out_ld < 1) return fail(LDB_ERR_SHAPE, "ct_normalize: out_ld must be positive");
+  const int threads = 256;
+  return launch_kernel(ct_normalize_kernel, dim3(static_cast<unsigned>((n + threads - 1) / threads)), dim3(threads), 0,
+                       stream, "ct_normalize launch", hu, n, out, int(out_dtype == LDB_F32), out_ld);
 }
 
 int ldb_step_advance(cudaStream_t stream, int* step) {

@@ -184,4 +184,10 @@ int ldb_version(void) { return LDB_ABI_VERSION; }
 
 unsigned long long ldb_launch_count(void) { return ldb::g_launches.load(std::memory_order_relaxed); }
 
+int ldb_clear_async(cudaStream_t stream, void* ptr, size_t bytes) {
+  if (!ptr && bytes) return ldb::fail(LDB_ERR_INVALID, "clear: null pointer");
+  if (!bytes) return LDB_OK;
+  return ldb::check_cuda(cudaMemsetAsync(ptr, 0, bytes, stream), "clear (memset)");
+}
+
 }  // extern "C"

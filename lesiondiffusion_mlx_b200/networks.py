@@ -129,14 +129,24 @@ class _Layers:
     def __init__(self, params: _Params):
         self.p = params
         self.exact = params.dtype == torch.float32
-        # Per-forward float64 arena (zeroed once per forward) that conv outputs
-        # feeding a GroupNorm take their statistics slices from.
+        # Float64 arena that conv outputs feeding a GroupNorm take their
+        # statistics slices from: allocated once per (batch, device) and
+        # cleared by a memset at the start of every forward (a memset node in
+        # a captured step, no kernel).
         self._arena: torch.Tensor | None = None
+        self._arenas: dict[tuple[int, torch.device], torch.Tensor] = {}
         self._arena_pos = 0
         self._stats_channels = sum(int(w.shape[0]) for w in params.raw.values() if w.ndim == 5)
 
     def _begin_stats(self, batch: int, device: torch.device) -> None:
-        self._arena = torch.zeros(batch * self._stats_channels * 2, dtype=torch.float64, device=device)
+        key = (batch, device)
+        arena = self._arenas.get(key)
+        if arena is None:
+            arena = torch.empty(batch * self._stats_channels * 2, dtype=torch.float64, device=device)
+            self._arenas[key] = arena
+        _lib.call("ldb_clear_async", torch.cuda.current_stream(device).cuda_stream, arena.data_ptr(),
+                  arena.numel() * arena.element_size())
+        self._arena = arena
         self._arena_pos = 0
 
     def _take_stats(self, batch: int, channels: int) -> torch.Tensor | None:
@@ -435,15 +445,20 @@ class VqDecoderB200(_Layers):
     ``levels`` lists decoder levels from the top (first run) down with
     ``(blocks, upsample_after)``; the reference's LINet VQ is 3 levels with
     one upsample after level 1 (the default).  ``scaled`` selects the
-    scaled-f16 decode of ScaledVqDecoder (_scaled_vq.py:27-118).
+    scaled-f16 decode of ScaledVqDecoder (_scaled_vq.py:27-118).  float32
+    weights run the reference's FP32 conditioned decode (medmlx.py:1374-1379,
+    ``decoder_mode="reference"``): FP32 quantize, FP32-exact split-f16 convs,
+    f32 activations.
     """
 
     SCALE = 0.25
 
     def __init__(self, weights: dict[str, torch.Tensor], *, device: torch.device | str = "cuda",
                  dtype: torch.dtype = torch.float16, groups: int = 16, scaled: bool = False):
-        if dtype != torch.float16:
-            raise ValueError("the B200 decoder runs in float16")
+        if dtype not in (torch.float16, torch.float32):
+            raise ValueError("the B200 decoder runs in float16 or float32")
+        if scaled and dtype != torch.float16:
+            raise ValueError("the scaled decoder is the float16 one")
         super().__init__(_Params(weights, torch.device(device), dtype))
         self.device = torch.device(device)
         self.groups = groups
@@ -454,7 +469,7 @@ class VqDecoderB200(_Layers):
         self.blocks = {lvl: sorted({int(m.group(1)) for n in names
                                     if (m := re.match(rf"decoder\.up\.{lvl}\.block\.(\d+)\.", n))})
                        for lvl in self.levels}
-        self.codebook = weights["quantize.embedding.weight"].to(self.device, torch.float16).contiguous()
+        self.codebook = weights["quantize.embedding.weight"].to(self.device, dtype).contiguous()
         for name in names:
             if name.endswith(".weight") and weights[name].ndim == 5:
                 self.p.conv(name[: -len(".weight")])
@@ -476,7 +491,10 @@ class VqDecoderB200(_Layers):
         return q
 
     def decode(self, z: torch.Tensor, *, quantize: bool = True, to_hu: bool = False) -> torch.Tensor:
-        """Decode NDHWC f16 latent ``z`` (B, d, h, w, C) to (B, 2d, 2h, 2w, C_out) (mlx_model.py:805-819)."""
+        """Decode NDHWC latent ``z`` (B, d, h, w, C) in the decoder's dtype to (B, 2d, 2h, 2w, C_out)
+        (mlx_model.py:805-819)."""
+        if z.dtype != self.p.dtype:
+            raise ValueError(f"latent dtype {z.dtype} != decoder dtype {self.p.dtype}")
         x = self.quantize(z) if quantize else z
         self._begin_stats(int(z.shape[0]), z.device)
         x = self.conv(x, "post_quant_conv")

@@ -352,6 +352,16 @@ def hu_map(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def ct_normalize(hu: torch.Tensor, *, out_dtype: torch.dtype = torch.float16, pad_to: int = 8) -> torch.Tensor:
+    """HU volume ``(B, D, H, W)`` (f32, contiguous) -> normalized NDHWC ``(B, D, H, W, 1)``
+    in ``out_dtype`` whose channel stride is ``pad_to`` (a conv input), padding zero."""
+    if hu.device.type != "cuda" or hu.dtype != torch.float32 or not hu.is_contiguous():
+        raise ValueError("ct_normalize expects a contiguous float32 CUDA HU tensor")
+    buf = torch.zeros((*hu.shape, pad_to), dtype=out_dtype, device=hu.device)
+    _lib.call("ldb_ct_normalize", _stream(hu), hu.data_ptr(), hu.numel(), buf.data_ptr(), _DT[out_dtype], pad_to)
+    return buf[..., :1]
+
+
 def step_advance(step: torch.Tensor) -> None:
     """Increment the device step counter (int32 scalar tensor)."""
     _lib.call("ldb_step_advance", _stream(step), step.data_ptr())

@@ -96,5 +96,5 @@ def test_other_operator_argument_errors():
         api.nearest_codebook4(torch.zeros((10, 3)), torch.zeros((5, 3)))
     with pytest.raises(ValueError, match="three spatial axes"):
         api.resize_nearest(torch.zeros((1, 1, 2, 2, 2)), (4, 4))
-    with pytest.raises(NotImplementedError):
-        api.piecewise_ct(torch.zeros(3), inverse=False)
+    with pytest.raises(ValueError, match="CUDA"):
+        api.piecewise_ct(torch.zeros(3), inverse=False)  # device kernels take device tensors only

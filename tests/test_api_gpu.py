@@ -184,7 +184,10 @@ def test_upsample_nearest2_and_resize_nearest(cuda_device):
     assert torch.equal(down.cpu(), oops.resize_nearest(xf, (4, 5, 3)))
 
 
-def test_piecewise_ct_inverse(cuda_device):
+def test_piecewise_ct_both_directions(cuda_device):
+    """Normalized -> HU and HU -> normalized, knots and clipping included, as the
+    oracle's restatement of mlx_pipeline.py:72-96 (FP32 arithmetic: exact up to
+    the last bit of the slope product)."""
     from lesiondiffusion_mlx_b200 import api
 
     values = np.concatenate([np.linspace(-0.5, 1.5, 4001), [0.0, 0.2, 0.8, 1.0]]).astype(np.float32)
@@ -194,8 +197,12 @@ def test_piecewise_ct_inverse(cuda_device):
     want = oops.piecewise_ct(x, inverse=True)
     assert hu.dtype == torch.float32 and tuple(hu.shape) == tuple(x.shape)
     np.testing.assert_allclose(hu.cpu().numpy(), want.numpy(), rtol=0, atol=1e-3)
-    with pytest.raises(NotImplementedError):
-        api.piecewise_ct(x.to(cuda_device), None, inverse=False)
+    hu_in = np.concatenate([np.linspace(-1500, 1500, 6001), [-1000, -200, 200, 1000]]).astype(np.float32)
+    h = torch.from_numpy(hu_in.reshape(5, 1201))
+    norm = api.piecewise_ct(h.to(cuda_device), None)
+    torch.cuda.synchronize()
+    assert norm.dtype == torch.float32 and tuple(norm.shape) == tuple(h.shape)
+    np.testing.assert_allclose(norm.cpu().numpy(), oops.piecewise_ct(h).numpy(), rtol=0, atol=1e-7)
 
 
 def test_nax_available_on_the_gpu_box(cuda_device):
