@@ -49,6 +49,14 @@ def partition_depth(depth: int, parts: int) -> list[tuple[int, int]]:
 class LocalDepthComm:
     """All slabs in this process: halo exchange by copies, statistics summed."""
 
+    def exchange_begin(self, bufs: list[torch.Tensor]):
+        """Start the halo exchange (here: done at once by stream-ordered copies)."""
+        self.exchange(bufs)
+        return None
+
+    def exchange_end(self, handle) -> None:
+        """Wait for the exchange begun by ``exchange_begin``."""
+
     def exchange(self, bufs: list[torch.Tensor]) -> None:
         """``bufs[i]`` (1, d_i + 2, H, W, ld): fill the halo slices from the neighbours."""
         for i, buf in enumerate(bufs):
@@ -103,8 +111,15 @@ class DistDepthComm:
         return self.dist.get_global_rank(self.group, r) if self.group is not None else r
 
     def exchange(self, bufs: list[torch.Tensor]) -> None:
+        self.exchange_end(self.exchange_begin(bufs))
+
+    def exchange_begin(self, bufs: list[torch.Tensor]):
+        """Post the grouped sends and receives of the halo slices and return
+        their requests: NCCL runs them on its own stream after the work already
+        on the current stream, so kernels launched before ``exchange_end``
+        overlap them (they must not read the halo slices or write the
+        boundary slices)."""
         (buf,) = bufs
-        end = self._span("exchange")
         dist = self.dist
         p2p = []
         # Same order on every rank: towards rank - 1 first, then towards rank + 1.
@@ -118,9 +133,14 @@ class DistDepthComm:
             last = int(buf.shape[1]) - 1
             p2p.append(dist.P2POp(dist.isend, _slice(buf, last - 1), self._peer(self.rank + 1), self.group))
             p2p.append(dist.P2POp(dist.irecv, _slice(buf, last), self._peer(self.rank + 1), self.group))
-        if p2p:
-            for req in dist.batch_isend_irecv(p2p):
-                req.wait()
+        return dist.batch_isend_irecv(p2p) if p2p else []
+
+    def exchange_end(self, handle) -> None:
+        """Make the current stream wait for the posted exchange (the span the
+        decode waits is what ``comm_ms`` reports as exchange time)."""
+        end = self._span("exchange")
+        for req in handle:
+            req.wait()
         if end is not None:
             end.record()
 
@@ -181,18 +201,45 @@ class ShardedVqDecoder:
 
     def _conv(self, src: list[_Slab], key: str, *, halo: bool, residual: list[_Slab] | None = None,
               output_scale: float = 1.0, stats: bool = True) -> list[_Slab]:
-        """Conv ``key`` of every slab into new slabs; 3x3x3 / up convs read the halo."""
+        """Conv ``key`` of every slab into new slabs; 3x3x3 / up convs read the halo.
+
+        With a halo the exchange runs under the slab's interior: output slices
+        1 .. d - 2 read only the slab's own slices, so that conv is launched
+        while the boundary slices travel; after the exchange the two boundary
+        output slices (which read a halo slice each) follow.  Slabs of fewer
+        than three slices wait for the exchange and run one conv."""
         packed = self.p.conv(key)
         up = 2 if packed.kind == "up" else 1
-        if halo:
-            self.comm.exchange([s.buf for s in src])
+        bias = self.p.f32(key + ".bias")
         out = self._new(src, packed.out_channels, up)
-        for i, (s, o) in enumerate(zip(src, out)):
+        for o in out:
             if stats:
-                o.stats = torch.zeros((1, packed.out_channels, 2), dtype=torch.float64, device=s.buf.device)
-            conv3d_ndhwc(s.full if halo else s.x, packed, self.p.f32(key + ".bias"), out=o.x,
-                         residual=None if residual is None else residual[i].x, output_scale=output_scale,
-                         stats=o.stats, depth_halo=1 if halo else 0)
+                o.stats = torch.zeros((1, packed.out_channels, 2), dtype=torch.float64, device=o.buf.device)
+        res = [None] * len(src) if residual is None else [r.x for r in residual]
+
+        def run(s: _Slab, o: _Slab, r, first: int, last: int) -> None:
+            """Output slices [first, last) of the slab from input slices [first, last + 2) of its halo buffer."""
+            conv3d_ndhwc(s.full[:, first:last + 2], packed, bias, out=o.x[:, up * first:up * last],
+                          residual=None if r is None else r[:, up * first:up * last], output_scale=output_scale,
+                          stats=o.stats, depth_halo=1)
+
+        if not halo:
+            for s, o, r in zip(src, out, res):
+                conv3d_ndhwc(s.x, packed, bias, out=o.x, residual=r, output_scale=output_scale, stats=o.stats)
+            return out
+        handle = self.comm.exchange_begin([s.buf for s in src])
+        split = all(int(s.x.shape[1]) >= 3 for s in src)
+        if split:
+            for s, o, r in zip(src, out, res):
+                run(s, o, r, 1, int(s.x.shape[1]) - 1)
+        self.comm.exchange_end(handle)
+        for s, o, r in zip(src, out, res):
+            d = int(s.x.shape[1])
+            if split:
+                run(s, o, r, 0, 1)
+                run(s, o, r, d - 1, d)
+            else:
+                run(s, o, r, 0, d)
         return out
 
     def _norm(self, src: list[_Slab], key: str, *, eps: float, voxels: int) -> list[_Slab]:
