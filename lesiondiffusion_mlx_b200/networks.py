@@ -239,6 +239,7 @@ class LdmUnetB200(_Layers):
         super().__init__(_Params(weights, torch.device(device), dtype))
         self.config = config
         self.device = torch.device(device)
+        self._side_streams: dict[torch.device, torch.cuda.Stream] = {}
         self.in_channels = int(weights["input_blocks.0.0.weight"].shape[1])
         self.out_channels = int(weights["out.2.weight"].shape[0])
         self._pack_all()
@@ -317,6 +318,8 @@ class LdmUnetB200(_Layers):
         """mlx_model.py:420-441 (with the skip concatenation [x | x2] fused into the norm pass).
 
         ``emb`` is the stacked per-block shift table from ``block_shifts``."""
+        if not self.exact and self.p.has(key + ".skip_connection.weight"):
+            return self._residual_with_skip_branch(x, emb, key, x2)
         channels = int(x.shape[-1]) + (0 if x2 is None else int(x2.shape[-1]))
         groups = 32 if channels % 32 == 0 else channels
         lo, hi = self._emb_offsets[key]
@@ -334,6 +337,46 @@ class LdmUnetB200(_Layers):
             skip = self.conv(cat, key + ".skip_connection")
         else:
             skip = x
+        return self.norm_silu_conv(h, key + ".out_layers.0", key + ".out_layers.3", groups=groups, eps=1e-5,
+                                   residual=skip, stats=True)
+
+    def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        stream = self._side_streams.get(device)
+        if stream is None:
+            stream = torch.cuda.Stream(device)
+            self._side_streams[device] = stream
+        return stream
+
+    def _residual_with_skip_branch(self, x: torch.Tensor, emb: torch.Tensor, key: str,
+                                   x2: torch.Tensor | None) -> torch.Tensor:
+        """``residual`` for f16 blocks with a 1x1 skip projection: the skip branch
+        (the [x | x2] copy and the projection) runs on a side stream while the
+        main stream normalizes and convolves, and joins before the second conv
+        adds it.  Its buffers are allocated on the main stream first, so the
+        allocator never frees memory one stream still uses."""
+        main = torch.cuda.current_stream(x.device)
+        side = self._side_stream(x.device)
+        packed = self.p.conv(key + ".skip_connection")
+        b, d, hh, ww, c1 = (int(v) for v in x.shape)
+        cin = c1 + (0 if x2 is None else int(x2.shape[-1]))
+        cat = None
+        if x2 is not None:
+            cat = torch.empty((b, d, hh, ww, (cin + 7) // 8 * 8), dtype=torch.float16, device=x.device)
+        cout = packed.out_channels
+        skip = torch.empty((b, d, hh, ww, (cout + 7) // 8 * 8), dtype=torch.float16, device=x.device)[..., :cout]
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            src = x if cat is None else ops.prepare_input(x, x2=x2, out=cat)
+            conv3d_ndhwc(src, packed, self.p.f32(key + ".skip_connection.bias"), out=skip, in_channels=cin)
+        channels = cin
+        groups = 32 if channels % 32 == 0 else channels
+        lo, hi = self._emb_offsets[key]
+        shift = emb[:, lo:hi].contiguous()
+        h = self.norm_silu_conv(x, key + ".in_layers.0", key + ".in_layers.2", groups=groups, eps=1e-5,
+                                shift=shift, x2=x2, stats=True)
+        out_c = int(h.shape[-1])
+        groups = 32 if out_c % 32 == 0 else out_c
+        main.wait_stream(side)
         return self.norm_silu_conv(h, key + ".out_layers.0", key + ".out_layers.3", groups=groups, eps=1e-5,
                                    residual=skip, stats=True)
 

@@ -109,7 +109,7 @@ def run_linet(image_hu, lesion: np.ndarray, nets: LinetNetworks, *, context: tor
               sampler: str = "ddim", steps: int = 200, crop: tuple[int, int, int] = LINET_CROP,
               initial_noise: torch.Tensor | None = None, step_noise: torch.Tensor | None = None,
               generator: torch.Generator | None = None, output_region: str = "box", graph: bool = True,
-              ) -> tuple[torch.Tensor, torch.Tensor | None, dict]:
+              keep_latent: bool = False) -> tuple[torch.Tensor, torch.Tensor | None, dict]:
     """One LINet draw on an even-sized source volume.
 
     ``image_hu`` is the (D, H, W) float32 CT in HU (NumPy or a CUDA tensor),
@@ -118,7 +118,9 @@ def run_linet(image_hu, lesion: np.ndarray, nets: LinetNetworks, *, context: tor
     inject the sampler's noise in the window's NDHWC layout (the reference's
     hooks, mlx_sampling.py:66-69); otherwise it is drawn from ``generator`` on
     the device.  Returns the generated CT in HU (D, H, W), the decode of the
-    unmodified latent for ``output_region="lesion"`` (else None), and stage facts.
+    unmodified latent for ``output_region="lesion"`` (else None), and stage facts
+    (with ``keep_latent`` also the encoded latent and the latent after the
+    write-back, f16 NDHWC, as ``"encoded"`` and ``"latent"``).
     """
     if sampler not in ("ddim", "dpmpp_2m"):
         raise ValueError("LesionDiffusion sampler must be ddim or dpmpp_2m")
@@ -157,12 +159,14 @@ def run_linet(image_hu, lesion: np.ndarray, nets: LinetNetworks, *, context: tor
         if sampler == "ddim":
             step_noise = torch.randn(prepared.state.noise.shape, generator=generator, device=device)
     generated = prepared.run(initial_noise, step_noise)
+    encoded = latent.clone() if keep_latent else None
     latent[sel] = generated.to(torch.float16)
     if not bool(torch.isfinite(latent).all()):
         raise FloatingPointError("LINet produced non-finite latents before quantization")
     torch.cuda.synchronize(device)
     sampled = time.perf_counter()
     # 5. decode to HU
+    written = latent.clone() if keep_latent else None
     generated_hu = _decode_hu(nets.decoder, latent)
     reconstruction_hu = None
     if output_region == "lesion":
@@ -177,4 +181,6 @@ def run_linet(image_hu, lesion: np.ndarray, nets: LinetNetworks, *, context: tor
         "input_reconstruction_decoded": reconstruction_hu is not None, "finite": True,
         "encode_and_sampling_s": sampled - started, "decode_s": time.perf_counter() - sampled,
     }
+    if keep_latent:
+        facts["encoded"], facts["latent"] = encoded, written
     return generated_hu, reconstruction_hu, facts
