@@ -813,11 +813,7 @@ __global__ void attn_sk_merge_kernel(const AttnParams p, unsigned int* status) {
 int choose_stream_k(long long ctas, int blocks, int* slots) {
   const int sms = sm_count();
   *slots = 0;
-  static const bool enabled = [] {
-    const char* v = std::getenv("LDB_ATTN_STREAMK");
-    return !(v && v[0] == '0');
-  }();
-  if (!enabled || ctas * 2 <= sms || blocks < 8) return 0;
+  if (ctas * 2 <= sms || blocks < 8) return 0;
   const long long waves = (ctas + sms - 1) / sms;
   if (ctas * 10 >= waves * sms * 9) return 0;  // the plain grid already fills 90 % of the waves
   const long long units = ctas * blocks;

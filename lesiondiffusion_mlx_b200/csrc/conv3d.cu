@@ -1285,34 +1285,6 @@ int dispatch_bn(int bn, cudaStream_t stream, const ConvMaps& maps, const CUtenso
   return fail(LDB_ERR_SHAPE, "no conv kernel for BN=%d", bn);
 }
 
-// The channel-major tile is on unless LDB_CONV_TRANS=0 (for comparisons).
-bool conv_trans_enabled() {
-  static const bool enabled = [] {
-    const char* v = std::getenv("LDB_CONV_TRANS");
-    return !(v && v[0] == '0');
-  }();
-  return enabled;
-}
-
-// CTA pairs for the 256-column tile are on unless LDB_CONV_PAIR=0 (for comparisons).
-bool conv_pair_enabled() {
-  static const bool enabled = [] {
-    const char* v = std::getenv("LDB_CONV_PAIR");
-    return !(v && v[0] == '0');
-  }();
-  return enabled;
-}
-
-// Tile-selection overrides for measurements (read on every plan): LDB_CONV_BN
-// (64 or 128) replaces the 256-column tile where the packed weight rows are
-// the same (out_channels a multiple of 256); LDB_CONV_SPLITS fixes the
-// split-K factor; LDB_CONV_TRANS_BD (1..3) the brick depth of the
-// channel-major tile.  Unset or 0: the planner's choice.
-int env_int(const char* name) {
-  const char* v = std::getenv(name);
-  return v ? std::atoi(v) : 0;
-}
-
 struct ConvPlan {
   int kc, bn, taps, cin_pad, grid;
   ConvParams p;
@@ -1348,10 +1320,6 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   else if (cout <= 64) bn = 64;
   else if (cout <= 128 || exact) bn = 128;
   else bn = 256;
-  {
-    const int force_bn = env_int("LDB_CONV_BN");
-    if (bn == 256 && cout % 256 == 0 && (force_bn == 64 || force_bn == 128)) bn = force_bn;
-  }
   if (d->depth_halo < 0 || d->depth_halo > 1) return fail(LDB_ERR_SHAPE, "depth_halo must be 0 or 1");
   const bool stride2 = d->mode == LDB_CONV_3X3X3_S2 || d->mode == LDB_CONV_3X3X3_S2_PAD01;
   if (d->depth_halo && stride2) return fail(LDB_ERR_SHAPE, "depth_halo with stride 2");
@@ -1391,8 +1359,7 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
       static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
   if (out_tiles > (1LL << 30)) return fail(LDB_ERR_SHAPE, "conv has too many tiles");
   const int sms = sm_count();
-  const int force_bn = env_int("LDB_CONV_BN");
-  if (taps == 1 && !exact && bn == 256 && cout % 256 == 0 && force_bn == 0) {
+  if (taps == 1 && !exact && bn == 256 && cout % 256 == 0) {
     // Pointwise: K is a few k-blocks, so split-K would only add a reduce
     // pass; fill the SMs with narrower column tiles instead.  Cost per tile
     // = k-blocks x shared-memory-bound k-block time ((128 + BN) x KC / 32
@@ -1417,7 +1384,7 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   // its 128-voxel brick and half of the 256 weight rows (32 KB per K block
   // instead of 48), so a stage carries 1.5x the FLOPs per staged byte and the
   // ring keeps more K blocks in flight.
-  const bool pair = !exact && bn == 256 && taps > 1 && bricks >= 2 && conv_pair_enabled();
+  const bool pair = !exact && bn == 256 && taps > 1 && bricks >= 2;
   // pairs of same-parity bricks (see pair_tile)
   const long long pairs = (bricks + 1) / 2 * p.parities;
   // CTAs one K range of every output tile needs (a pair's placeholder tile counts)
@@ -1426,10 +1393,6 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   if (taps > 1 && tiles_now < sms && p.kb_total >= 8) {
     splits = static_cast<int>(std::min<long long>(sms / tiles_now, p.kb_total / 4));
     splits = std::max(1, splits);
-  }
-  {
-    const int force_splits = env_int("LDB_CONV_SPLITS");
-    if (force_splits > 0) splits = std::min(force_splits, p.kb_total);
   }
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
@@ -1461,14 +1424,12 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   // kernels only: a pointwise conv has too few K blocks per tile to hide the
   // per-plane transposed epilogue, and its voxel-major tile runs ~3x faster.)
   const bool trans_ok = !exact && taps > 1 && p.k_splits == 1 && kc == 64 &&
-                        (cout == 128 || (cout == 64 && p.parities == 1)) && conv_trans_enabled();
+                        (cout == 128 || (cout == 64 && p.parities == 1));
   if (trans_ok) {
     const long long th = (gh + 7) / 8, tw = (gw + 7) / 8;
     int best_bd = 1;
     long long best_cost = -1;
-    const int force_bd = env_int("LDB_CONV_TRANS_BD");  // tuning override, 1..3
     for (int cand = 1; cand <= 3; ++cand) {
-      if (force_bd >= 1 && force_bd <= 3 && cand != force_bd) continue;
       const long long tiles = static_cast<long long>(B) * ((gd + cand - 1) / cand) * th * tw * p.parities;
       const long long cost = ((tiles + sms - 1) / sms) * (64LL * cand + 64);
       if (best_cost < 0 || cost <= best_cost) {

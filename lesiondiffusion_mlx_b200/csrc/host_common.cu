@@ -73,14 +73,6 @@ int sm_count() {
   return cache[dev];
 }
 
-bool pdl_enabled() {
-  static const bool enabled = [] {
-    const char* v = std::getenv("LDB_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return enabled;
-}
-
 void count_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
 
 int ensure_smem_attribute(const void* kernel, int bytes, unsigned long long* flags, const char* what) {

@@ -32,10 +32,6 @@ unsigned int* device_status_ptr();
 // Count one kernel launch issued by the library (see ldb_launch_count).
 void count_launch(int n = 1);
 
-// Whether kernels are launched with programmatic stream serialization
-// (default on; LDB_PDL=0 in the environment turns it off).
-bool pdl_enabled();
-
 // Launch `kernel` (every library kernel starts with pdl_begin()) with
 // programmatic stream serialization, count it, and map a launch failure to
 // LDB_ERR_CUDA with `what` in the message.
@@ -51,7 +47,7 @@ int launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   count_launch();
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...), what);
 }
@@ -74,7 +70,7 @@ int launch_kernel_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.numAttrs = 2;
   count_launch();
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...), what);
 }
