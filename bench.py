@@ -357,6 +357,14 @@ def main() -> None:
         timed_graph.replay()
     torch.cuda.synchronize()
     kernel = timer.summary()
+    # the conv launches by kind: 3x3x3 (strided and folded-up included) and pointwise / dense
+    conv_kinds: dict[str, list[float]] = {}
+    for kind, label, flops, ms in timer.launches():
+        if kind == "conv3d":
+            entry = conv_kinds.setdefault("pointwise" if label.startswith("mode3 ") else "3x3x3", [0, 0.0, 0.0])
+            entry[0] += 1
+            entry[1] += ms
+            entry[2] += flops
     elapsed_ms = _max_over_ranks(elapsed_ms, world, device)
     trajectory_ms = _max_over_ranks(trajectory_ms, world, device)
     decode_ms = _max_over_ranks(decode_ms, world, device)
@@ -428,6 +436,12 @@ def main() -> None:
                 "frac_of_sustained": (conv_tflops / peak_sustained) if conv_tflops else None,
                 "traffic": traffic,
                 "flops_per_step": conv["flops"], "launches_per_step": conv["launches"], "ms_per_step": conv["ms"],
+                "by_kind": {
+                    name: {"launches": n, "ms_per_step": round(ms, 4),
+                           "achieved": flops / (ms * 1e-3) / 1e12 if ms else None,
+                           "frac": flops / (ms * 1e-3) / 1e12 / peak_burst if ms else None}
+                    for name, (n, ms, flops) in sorted(conv_kinds.items())
+                },
             },
             "attention": {"achieved_tflops": attn_tflops, "frac": (attn_tflops / peak_burst) if attn_tflops else None,
                           "flops_per_step": attn["flops"], "ms_per_step": attn["ms"], "launches": attn["launches"]},

@@ -28,6 +28,7 @@
 // reference's SPLIT/reduce kernels (_nax_conv.py:277-289, :556-563).
 
 #include <algorithm>
+#include <climits>
 #include <cstdlib>
 #include <cstring>
 
@@ -1291,6 +1292,26 @@ struct ConvPlan {
   size_t workspace;
 };
 
+// A pointwise conv over whole volumes is a GEMM over their voxels: it is
+// planned as a 1 x 1 x (D H W) row of voxels (the voxel stride unchanged),
+// so every tile is a run of 128 voxels instead of a box brick whose last
+// rows and columns fall past the volume.  Other descriptors (and ones whose
+// struct_size the planner will reject) pass through unchanged.
+const ldb_conv_desc* flat_pointwise(const ldb_conv_desc* d, ldb_conv_desc* tmp) {
+#ifndef LDB_CONV_FLAT_PW
+#define LDB_CONV_FLAT_PW 1
+#endif
+  if (!LDB_CONV_FLAT_PW || !d || d->struct_size != static_cast<int>(sizeof(ldb_conv_desc))) return d;
+  if (d->mode != LDB_CONV_1X1 || d->depth_halo != 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0) return d;
+  const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
+  if (voxels > INT_MAX || (d->depth == 1 && d->height == 1)) return d;
+  *tmp = *d;
+  tmp->depth = 1;
+  tmp->height = 1;
+  tmp->width = static_cast<int>(voxels);
+  return tmp;
+}
+
 int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   if (!d) return fail(LDB_ERR_INVALID, "conv descriptor is null");
   if (d->struct_size != static_cast<int>(sizeof(ldb_conv_desc)))
@@ -1465,6 +1486,8 @@ extern "C" {
 
 int ldb_conv3d_workspace_size(const ldb_conv_desc* desc, size_t* bytes) {
   if (!bytes) return ldb::fail(LDB_ERR_INVALID, "bytes pointer is null");
+  ldb_conv_desc flat;
+  desc = ldb::flat_pointwise(desc, &flat);
   ldb::ConvPlan plan;
   int rc = ldb::plan_conv(desc, &plan);
   if (rc != LDB_OK) return rc;
@@ -1473,6 +1496,8 @@ int ldb_conv3d_workspace_size(const ldb_conv_desc* desc, size_t* bytes) {
 }
 
 int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_parity, int* k_total) {
+  ldb_conv_desc flat;
+  desc = ldb::flat_pointwise(desc, &flat);
   ldb::ConvPlan plan;
   int rc = ldb::plan_conv(desc, &plan);
   if (rc != LDB_OK) return rc;
@@ -1485,6 +1510,8 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
                         const float* bias, const float* shift, const void* residual, void* out, double* stats,
                         void* workspace, size_t workspace_bytes) {
   using namespace ldb;
+  ldb_conv_desc flat;
+  desc = flat_pointwise(desc, &flat);
   ConvPlan plan;
   int rc = plan_conv(desc, &plan);
   if (rc != LDB_OK) return rc;

@@ -195,6 +195,34 @@ def test_pointwise_conv_and_gelu(cuda_device, shape, out_channels):
     assert np.all(np.abs(gelu_actual - gelu_expected) <= 2 * half_spacing(gelu_expected) + 1e-6)
 
 
+@pytest.mark.parametrize("shape,out_channels", [((2, 96, 3, 5, 7), 256), ((1, 64, 4, 9, 10), 128),
+                                                ((2, 32, 1, 1, 200), 48)])
+def test_pointwise_conv_over_flat_voxel_rows(cuda_device, shape, out_channels):
+    """Pointwise convs are planned over each volume's voxels as one row (tiles
+    of 128 consecutive voxels, the last one partial): per-batch shift,
+    residual and the GroupNorm statistics of the stored output stay exact."""
+    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_weight
+
+    x, w, b = f16_case(shape, out_channels, 1, seed=sum(shape) + 3 * out_channels)
+    batch = shape[0]
+    rng = np.random.default_rng(17)
+    shift = torch.from_numpy(rng.normal(size=(batch, out_channels)).astype(np.float32) * 0.1)
+    residual = torch.from_numpy(rng.normal(size=(batch, out_channels, *shape[2:])).astype(np.float16))
+    stats = torch.zeros((batch, out_channels, 2), dtype=torch.float64, device=cuda_device)
+    out = conv3d_ndhwc(to_ndhwc(x.to(cuda_device)), pack_weight(w.to(cuda_device)), b.to(cuda_device).float(),
+                       shift=shift.to(cuda_device), residual=to_ndhwc(residual.to(cuda_device)).contiguous(),
+                       stats=stats)
+    torch.cuda.synchronize()
+    actual = out.permute(0, 4, 1, 2, 3).double().cpu().numpy()
+    products, mag = reference(x.double(), w.double(), b.double(), 1, 0)
+    expected = products + shift.double().numpy()[:, :, None, None, None] + residual.double().numpy()
+    error = np.abs(actual - expected)
+    assert np.all(error <= half_spacing(expected) + ACCUMULATION_EPS * mag), f"max excess {error.max()}"
+    sums = actual.reshape(batch, out_channels, -1)
+    want = np.stack([sums.sum(-1), (sums * sums).sum(-1)], axis=-1)
+    np.testing.assert_allclose(stats.cpu().numpy(), want, rtol=1e-5, atol=1e-3)
+
+
 @pytest.mark.parametrize(
     ("shape", "out_channels", "kind", "extra"),
     [
