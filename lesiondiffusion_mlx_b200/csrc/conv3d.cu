@@ -1298,10 +1298,7 @@ struct ConvPlan {
 // rows and columns fall past the volume.  Other descriptors (and ones whose
 // struct_size the planner will reject) pass through unchanged.
 const ldb_conv_desc* flat_pointwise(const ldb_conv_desc* d, ldb_conv_desc* tmp) {
-#ifndef LDB_CONV_FLAT_PW
-#define LDB_CONV_FLAT_PW 1
-#endif
-  if (!LDB_CONV_FLAT_PW || !d || d->struct_size != static_cast<int>(sizeof(ldb_conv_desc))) return d;
+  if (!d || d->struct_size != static_cast<int>(sizeof(ldb_conv_desc))) return d;
   if (d->mode != LDB_CONV_1X1 || d->depth_halo != 0 || d->depth <= 0 || d->height <= 0 || d->width <= 0) return d;
   const long long voxels = static_cast<long long>(d->depth) * d->height * d->width;
   if (voxels > INT_MAX || (d->depth == 1 && d->height == 1)) return d;
