@@ -864,7 +864,7 @@ int launch_attn(cudaStream_t stream, const CUtensorMap& qm, const CUtensorMap& k
   int r = launch_kernel(kernel, grid, dim3(kAttnThreads), Cfg::kSmemBytes, stream, "attention launch", qm, km, vm,
                         p, device_status_ptr());
   if (r != LDB_OK) return r;
-  if (p.sk_ctas > 0) {
+  if (p.sk_ctas > 0 && p.sk_nb > 1) {  // (with one key block every unit is whole)
     using OutT = typename std::conditional<SPLIT, float,
                                            typename std::conditional<BF16, __nv_bfloat16, __half>::type>::type;
     const long long blocks = p.sk_units / p.sk_nb * (2 * kBlockM / kMergeRows);
@@ -953,6 +953,15 @@ static int flash_attention_impl(cudaStream_t stream, const void* q, int q_ld, co
       p.o_part = static_cast<float*>(workspace);
       p.ml_part = p.o_part + sk_rows * head_dim;
     }
+  }
+  // Short keys (one key block) on a grid of more than one wave: a persistent
+  // grid of one CTA per SM over the (query pair, head) units, in contiguous
+  // ranges, so a CTA's set-up is paid once and its next unit's queries load
+  // while it finishes the current one.  Every unit is whole: nothing to merge.
+  if (p.sk_ctas == 0 && p.kv_splits == 1 && blocks == 1 && ctas > sm_count()) {
+    p.sk_ctas = sm_count();
+    p.sk_nb = 1;
+    p.sk_units = ctas;
   }
   if (head_dim == 64) return bf16 ? launch_attn<64, true>(stream, qm, km, vm, p) : launch_attn<64, false>(stream, qm, km, vm, p);
   if (head_dim == 32) return bf16 ? launch_attn<32, true>(stream, qm, km, vm, p) : launch_attn<32, false>(stream, qm, km, vm, p);

@@ -147,7 +147,8 @@ def test_flash_attention_f32(cuda_device, batch, lq, lk, heads, qscale, d):
         (1, 640, 77, 8, 64, torch.float16, False),  # cross-attention, one partial key block
         (2, 300, 200, 4, 64, torch.bfloat16, False),
         (1, 6400, 6400, 8, 64, torch.bfloat16, False),  # config-2 self-attention
-        (1, 6400, 77, 8, 64, torch.bfloat16, False),  # config-2 cross-attention
+        (1, 6400, 77, 8, 64, torch.bfloat16, False),  # config-2 cross-attention: 200 units, persistent grid
+        (3, 2000, 100, 12, 64, torch.float16, False),  # short keys, persistent grid across batches and heads
         (1, 6400, 6400, 4, 64, torch.float16, False),  # stream-K: 100 pairs on all SMs, 2 segments per CTA
         (1, 4000, 1000, 16, 64, torch.float16, False),  # stream-K, up to 3 segments per CTA, partial tiles
     ],
