@@ -253,7 +253,7 @@ def main() -> None:
 
     from lesiondiffusion_mlx_b200 import _lib, instrument, ops, vq_bench, workloads
     from lesiondiffusion_mlx_b200.networks import LdmUnetB200, VqDecoderB200
-    from lesiondiffusion_mlx_b200.sampling import DdimSampler, PreparedSampler
+    from lesiondiffusion_mlx_b200.sampling import DdimSampler, HostStreamedSteps, PreparedSampler
 
     dist = None
     if world > 1:
@@ -373,12 +373,14 @@ def main() -> None:
     ms_per_step = elapsed_ms / args.steps
     value = world * args.steps / (elapsed_ms / 1e3)
 
-    # End to end through the public step API with host buffers: per step the
-    # step's noise comes from pinned host memory and the updated latent is
-    # read back to the host.
+    # End to end through the public step API with host buffers: every step
+    # the step's noise comes from pinned host memory and the updated latent is
+    # read back to pinned host memory (HostStreamedSteps: the copies run on a
+    # copy stream beside the neighbouring steps' compute).
     host_noise = noise[0].cpu().pin_memory()
     host_out = torch.empty(prepared.state.x.shape, dtype=torch.float32).pin_memory()
     prepared.begin(init, noise)
+    streamer = HostStreamedSteps(prepared, step=graph.replay)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -386,12 +388,12 @@ def main() -> None:
     e_end = torch.cuda.Event(enable_timing=True)
     e_steps = args.steps
     e_start.record(stream)
+    streamer.start(host_noise)
     for i in range(e_steps):
         if i and i % sampler.steps == 0:
-            prepared.begin(init, noise)
-        prepared.state.noise[i % sampler.steps].copy_(host_noise, non_blocking=True)
-        graph.replay()
-        host_out.copy_(prepared.state.x, non_blocking=True)
+            prepared.begin(init)  # a trajectory finished: restart its state (the noise slots stay the stream's)
+        streamer.step(host_noise if i + 1 < e_steps else None, host_out)
+    streamer.finish()
     e_end.record(stream)
     torch.cuda.synchronize()
     e_ms = _max_over_ranks(e_start.elapsed_time(e_end), world, device)

@@ -232,3 +232,88 @@ class PreparedSampler:
         for _ in range(self.sampler.steps):
             self.step()
         return self.state.x
+
+
+class HostStreamedSteps:
+    """Steps a prepared sampler with host I/O every step: step i's noise is
+    copied in from pinned host memory and its updated latent copied out to
+    pinned host memory, both on a copy stream, so the copy-in of step i + 1
+    and the copy-out of step i - 1 run while step i computes.
+
+    Step i's noise goes to noise slot i mod steps (the slot the sampler reads
+    at step i of a trajectory that restarts every ``steps`` steps); a slot is
+    refilled only after the step that last read it has run.  The latent is
+    first copied into one of two device staging buffers (a device-to-device
+    copy on the compute stream) so that the next step can update it while
+    the host copy is in flight.  ``finish()`` makes the compute stream wait
+    for every copy; call it before ``PreparedSampler.begin`` with step noise,
+    which rewrites the noise slots.
+    """
+
+    def __init__(self, prepared: PreparedSampler, step=None):
+        self.prepared = prepared
+        self._run_step = step if step is not None else prepared.step  # e.g. a captured graph's replay
+        s = prepared.state
+        self.device = s.x.device
+        self.compute = torch.cuda.current_stream(self.device)
+        self.copy = torch.cuda.Stream(self.device)
+        self.stage = [torch.empty_like(s.x), torch.empty_like(s.x)]
+        self._in_done: dict[int, torch.cuda.Event] = {}
+        self._step_done: dict[int, torch.cuda.Event] = {}
+        self._out_done: list[torch.cuda.Event | None] = [None, None]
+        self._count = 0
+
+    def _copy_in(self, i: int, host_noise: torch.Tensor) -> None:
+        steps = self.prepared.sampler.steps
+        last_reader = self._step_done.pop(i - steps, None)  # the step that last read this slot
+        with torch.cuda.stream(self.copy):
+            if last_reader is not None:
+                self.copy.wait_event(last_reader)
+            self.prepared.state.noise[i % steps].copy_(host_noise, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.copy)
+        self._in_done[i] = ev
+
+    def start(self, host_noise: torch.Tensor) -> None:
+        """Begin the copy-in of the first step's noise (the sampler at step 0),
+        after all work already queued on the compute stream."""
+        self._count = 0
+        self._step_done.clear()
+        self.copy.wait_stream(self.compute)
+        self._copy_in(0, host_noise)
+
+    def step(self, next_host_noise: torch.Tensor | None, host_out: torch.Tensor) -> None:
+        """Run the next step (its noise copy already started), start the copy-in
+        of the following step's noise when given, and the copy-out of this
+        step's latent into ``host_out``."""
+        i = self._count
+        s = self.prepared.state
+        self.compute.wait_event(self._in_done.pop(i))
+        self._run_step()
+        done = torch.cuda.Event()
+        done.record(self.compute)
+        self._step_done[i] = done
+        if next_host_noise is not None:
+            self._copy_in(i + 1, next_host_noise)
+        buf = i & 1
+        if self._out_done[buf] is not None:
+            self.compute.wait_event(self._out_done[buf])  # the copy-out two steps back has read the buffer
+        self.stage[buf].copy_(s.x)
+        ready = torch.cuda.Event()
+        ready.record(self.compute)
+        with torch.cuda.stream(self.copy):
+            self.copy.wait_event(ready)
+            host_out.copy_(self.stage[buf], non_blocking=True)
+            out_done = torch.cuda.Event()
+            out_done.record(self.copy)
+        self._out_done[buf] = out_done
+        self._count = i + 1
+
+    def finish(self) -> None:
+        """Make the compute stream wait for every copy issued so far."""
+        for ev in self._out_done:
+            if ev is not None:
+                self.compute.wait_event(ev)
+        for ev in self._in_done.values():
+            self.compute.wait_event(ev)
+        self._in_done.clear()
