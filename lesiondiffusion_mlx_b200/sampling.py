@@ -75,7 +75,8 @@ class DdimSampler:
         sigmas = (f(eta) * np.sqrt(((f(1) - p32) * inverse_variance).astype(f) * (f(1) - (a32 / p32).astype(f)))).astype(f)
         self.alphas, self.previous, self.sigmas, self.sqrt_one_minus = a32, p32, sigmas, sqrt_one_minus
         table = np.stack([a32, p32, sigmas, sqrt_one_minus, np.zeros_like(a32)], axis=1)
-        self.coefficients = np.ascontiguousarray(table[::-1])
+        # a copy, not ascontiguousarray: a one-row reversed view counts as contiguous with a negative stride
+        self.coefficients = table[::-1].copy()
         self.execution_timesteps = tuple(reversed(self.timesteps))
 
     @property
@@ -172,7 +173,7 @@ class PreparedSampler:
             prev=torch.zeros((b, d, h, w, c), dtype=torch.float32, device=dev),
             net_in=net_in,
             noise=torch.zeros((steps, b, d, h, w, c), dtype=torch.float32, device=dev),
-            coeff=torch.from_numpy(np.ascontiguousarray(sampler.coefficients)).to(dev),
+            coeff=torch.from_numpy(np.array(sampler.coefficients, dtype=np.float32)).to(dev),
             timesteps=torch.tensor([[t] * b for t in sampler.execution_timesteps], dtype=torch.int32, device=dev),
             step=torch.zeros((), dtype=torch.int32, device=dev),
             mask=None if mask is None else mask.to(dev, torch.float32).reshape(b, d, h, w).contiguous(),

@@ -169,3 +169,17 @@ def test_sampler_tables_match_oracle():
     np.testing.assert_array_equal(p.coefficients, coeffs)
     with pytest.raises(ValueError):
         DdimSampler(acp, 3)
+
+
+def test_one_step_ddim_table_has_positive_strides():
+    """A one-step DDIM schedule's coefficient table (reversed into execution
+    order) is a real copy: torch cannot wrap a view with a negative stride."""
+    import torch
+
+    from lesiondiffusion_mlx_b200.sampling import DdimSampler
+
+    alphas = np.linspace(0.9999, 0.02, 1000).astype(np.float32)
+    for steps in (1, 2, 50):
+        table = DdimSampler(alphas, steps).coefficients
+        assert table.shape == (steps, 5) and all(s > 0 for s in table.strides)
+        assert torch.from_numpy(table).shape == (steps, 5)
