@@ -34,6 +34,7 @@ def test_host_streamed_steps_match_device_steps(cuda_device, steps):
     mask[:, 1:3, 2:6, 2:6] = 1.0
     alphas = np.linspace(0.9999, 0.02, 1000).astype(np.float32)
     sampler = DdimSampler(alphas, steps)
+    steps = sampler.steps  # steps the schedule executes (noise slots)
     prepared = PreparedSampler(sampler, unet, {}, image, mask.to(cuda_device), graph=False)
     s = prepared.state
     eps = torch.from_numpy(rng.standard_normal(tuple(s.x.shape)).astype(np.float32)).half().to(cuda_device)
