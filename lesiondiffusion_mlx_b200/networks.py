@@ -244,6 +244,7 @@ class LdmUnetB200(_Layers):
         self.out_channels = int(weights["out.2.weight"].shape[0])
         self._pack_all()
         self._stack_embedding_projections()
+        self._pack_dense()
 
     def _stack_embedding_projections(self) -> None:
         """Stack every residual block's ``emb_layers.1`` so one skinny GEMM per step
@@ -279,6 +280,29 @@ class LdmUnetB200(_Layers):
             if name.endswith(".norm.weight") or re.search(r"(in_layers\.0|out_layers\.0|norm[123]|out\.0)\.weight$", name):
                 self.p.f32(name)
                 self.p.f32(name[: -len("weight")] + "bias")
+
+    def _pack_dense(self) -> None:
+        """Pack the dense layers the forward pass uses (fused Q/K/V, Q alone when
+        a context gives K/V, the output and feed-forward projections, the time
+        and block embeddings), so that no step, eager or captured, packs."""
+        groups: list[tuple[str, ...]] = []
+        if self.exact:
+            groups += [("time_embed.0",), ("time_embed.2",), self._emb_keys]
+        else:
+            for key in ("time_embed.0", "time_embed.2"):
+                self.p.f16(key + ".weight")
+                self.p.f32(key + ".bias")
+        for name in self.p.raw:
+            if not name.endswith(".attn1.to_q.weight"):
+                continue
+            blk = name[: -len(".attn1.to_q.weight")]
+            for attn in (blk + ".attn1", blk + ".attn2"):
+                groups += [(attn + ".to_q", attn + ".to_k", attn + ".to_v"), (attn + ".to_q",), (attn + ".to_out.0",)]
+            groups += [(blk + ".ff.net.0.0",), (blk + ".ff.net.2",)]
+        for keys in groups:
+            if keys and all(k + ".weight" in self.p.raw for k in keys):
+                self.p.dense_packed(*keys)
+                self.p.dense_bias(*keys)
 
     # ------------------------------------------------------------- blocks
 
