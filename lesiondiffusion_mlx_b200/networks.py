@@ -300,9 +300,12 @@ class LdmUnetB200(_Layers):
                 groups += [(attn + ".to_q", attn + ".to_k", attn + ".to_v"), (attn + ".to_q",), (attn + ".to_out.0",)]
             groups += [(blk + ".ff.net.0.0",), (blk + ".ff.net.2",)]
         for keys in groups:
-            if keys and all(k + ".weight" in self.p.raw for k in keys):
-                self.p.dense_packed(*keys)
-                self.p.dense_bias(*keys)
+            if not keys or not all(k + ".weight" in self.p.raw for k in keys):
+                continue
+            if len({tuple(self.p.raw[k + ".weight"].shape[1:]) for k in keys}) != 1:
+                continue  # (cross-attention K/V read the context width: never fused with Q)
+            self.p.dense_packed(*keys)
+            self.p.dense_bias(*keys)
 
     # ------------------------------------------------------------- blocks
 
