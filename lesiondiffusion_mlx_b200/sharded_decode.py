@@ -34,13 +34,24 @@ from .networks import VqDecoderB200
 
 
 def partition_depth(depth: int, parts: int) -> list[tuple[int, int]]:
-    """Contiguous [start, stop) slabs of ``depth`` slices, sizes differing by at most one."""
+    """Contiguous [start, stop) slabs of ``depth`` slices, sizes differing by at most one.
+
+    The slices left over after an even split go to the end slabs first (slab
+    0, the last slab, then 1, the second to last, ...): an end slab exchanges
+    one halo per conv, an inner slab two, so the end slabs can take the extra
+    slice without becoming the slowest."""
     if parts <= 0 or depth < parts:
         raise ValueError(f"cannot split {depth} slices into {parts} non-empty slabs")
     base, extra = divmod(depth, parts)
+    order = [i for pair in zip(range(parts), reversed(range(parts))) for i in pair]
+    bigger = set()
+    for i in order:
+        if len(bigger) == extra:
+            break
+        bigger.add(i)
     out, start = [], 0
     for i in range(parts):
-        stop = start + base + (1 if i < extra else 0)
+        stop = start + base + (1 if i in bigger else 0)
         out.append((start, stop))
         start = stop
     return out
