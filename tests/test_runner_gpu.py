@@ -107,8 +107,9 @@ def _volume(shape=(16, 24, 24), seed=3) -> tuple[np.ndarray, np.ndarray]:
     return image, lesion
 
 
-@pytest.mark.parametrize("decoder_mode", ["reference", "scaled_fp16"])
-def test_run_linet_matches_oracle_composition(cuda_device, bundle, decoder_mode):
+@pytest.mark.parametrize("sampler,decoder_mode", [("ddim", "reference"), ("ddim", "scaled_fp16"),
+                                                   ("dpmpp_2m", "reference")])
+def test_run_linet_matches_oracle_composition(cuda_device, bundle, sampler, decoder_mode):
     from lesiondiffusion_mlx_b200 import runner
 
     path, config, unet_w, vq_w, alphas = bundle
@@ -123,7 +124,8 @@ def test_run_linet_matches_oracle_composition(cuda_device, bundle, decoder_mode)
     noise = rng.standard_normal((4, 1, 4, *wshape)).astype(np.float32)
     to_dev = lambda a: torch.from_numpy(np.ascontiguousarray(np.moveaxis(a, -4, -1))).to(cuda_device)  # noqa: E731
     gen_hu, recon_hu, facts = runner.run_linet(image, lesion, nets, context=torch.from_numpy(context), steps=4,
-                                               crop=crop, initial_noise=to_dev(init), step_noise=to_dev(noise),
+                                               sampler=sampler, crop=crop, initial_noise=to_dev(init),
+                                               step_noise=to_dev(noise) if sampler == "ddim" else None,
                                                output_region="lesion", keep_latent=True)
     ncdhw = lambda t: t.permute(0, 4, 1, 2, 3).contiguous().cpu()  # noqa: E731
     encoded_gpu, latent_gpu = ncdhw(facts["encoded"]), ncdhw(facts["latent"])
@@ -146,8 +148,13 @@ def test_run_linet_matches_oracle_composition(cuda_device, bundle, decoder_mode)
     def denoise(net_in, t, _condition):
         return oracle.forward(torch.from_numpy(net_in).to(torch.float16), torch.from_numpy(t), projected, kv).float()
 
-    x = osamp.ddim_sample(denoise, None, image_w, osamp.ddim_coefficients(alphas, 4), initial_noise=init,
-                          step_noise=noise, mask=mask_w)
+    if sampler == "ddim":
+        x = osamp.ddim_sample(denoise, None, image_w, osamp.ddim_coefficients(alphas, 4), initial_noise=init,
+                              step_noise=noise, mask=mask_w)
+    else:
+        ts, coeffs = osamp.dpm_coefficients(alphas, 4)
+        x = osamp.dpm_sample(lambda net_in, t: denoise(net_in, t, None), image_w, ts, coeffs, initial_noise=init,
+                             mask=mask_w)
     # generation: encoder latent and sampled window at the f16 bound
     assert rel_l2(encoded_gpu.float().numpy(), enc.float().numpy()) <= 1e-2
     assert rel_l2(latent_gpu[sel].float().numpy(), x) <= 1e-2
