@@ -24,6 +24,17 @@ def test_partition_depth_is_contiguous_and_balanced():
         partition_depth(3, 4)
 
 
+def test_partition_depth_gives_leftover_slices_to_the_end_slabs():
+    """An end slab exchanges one halo per conv, an inner slab two: the slices
+    left after an even split go to the end slabs first, then inwards."""
+    sizes = lambda depth, parts: [b - a for a, b in partition_depth(depth, parts)]  # noqa: E731
+    assert sizes(62, 4) == [16, 15, 15, 16]
+    assert sizes(62, 8) == [8, 8, 8, 7, 7, 8, 8, 8]
+    assert sizes(10, 3) == [4, 3, 3]
+    assert sizes(11, 3) == [4, 3, 4]
+    assert sizes(9, 3) == [3, 3, 3]
+
+
 def _volume(depth: int) -> torch.Tensor:
     # (1, depth, 3, 2, 8) with every slice distinct
     return torch.arange(depth * 3 * 2 * 8, dtype=torch.float32).reshape(1, depth, 3, 2, 8)
