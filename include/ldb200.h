@@ -36,7 +36,7 @@ extern "C" {
 
 typedef struct CUstream_st* ldb_stream_t; /* binary compatible with cudaStream_t */
 
-#define LDB_ABI_VERSION 2
+#define LDB_ABI_VERSION 3
 
 enum {
   LDB_OK = 0,
@@ -62,7 +62,8 @@ enum {
 enum { LDB_ACT_NONE = 0, LDB_ACT_GELU = 1 };
 
 /* Library ABI version (LDB_ABI_VERSION).  Version 2 added
- * ldb_conv_desc.struct_size as the descriptor's first field. */
+ * ldb_conv_desc.struct_size as the descriptor's first field, version 3
+ * ldb_conv_desc.max_ctas. */
 LDB_API int ldb_version(void);
 
 /* Number of kernels this library has launched (or recorded into a CUDA
@@ -122,6 +123,10 @@ typedef struct {
    * interior slices (twice that for LDB_CONV_UP2).  0 or 1; not with stride 2 (modes 1 and 4).
    * Used by the depth-sharded decode, where each GPU holds a slab. */
   int depth_halo;
+  /* Upper bound on the CTAs (SMs) the conv occupies; 0: all SMs.  Leaving a
+   * few SMs free lets a communication kernel running beside the conv (the
+   * halo exchange of the depth-sharded decode) make progress during it. */
+  int max_ctas;
   /* Optional device pointer to two 64-bit words (start, end) for timing the
    * launch from the device clock (%globaltimer, ns): the kernel lowers start
    * (atomic min) to the time its first CTA passes its dependency wait and

@@ -48,6 +48,7 @@ class ConvDesc(ctypes.Structure):
         ("act", ctypes.c_int),
         ("output_scale", ctypes.c_float),
         ("depth_halo", ctypes.c_int),
+        ("max_ctas", ctypes.c_int),
         ("clock", ctypes.c_void_p),
     ]
 

@@ -216,6 +216,7 @@ def conv3d_ndhwc(
     stats: torch.Tensor | None = None,
     depth_halo: int = 0,
     pad01: bool = False,
+    max_ctas: int = 0,
 ) -> torch.Tensor:
     """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
@@ -262,7 +263,7 @@ def conv3d_ndhwc(
         batch=batch, depth=depth, height=height, width=width, in_channels=cin, x_ld=x_ld,
         out_channels=cout, out_ld=out_ld, res_ld=res_ld, mode=mode, exact=int(packed.exact),
         out_dtype=_lib.LDB_F32 if out_dtype == torch.float32 else _lib.LDB_F16, act=act,
-        output_scale=float(output_scale), depth_halo=depth_halo,
+        output_scale=float(output_scale), depth_halo=depth_halo, max_ctas=int(max_ctas),
     )
     ws_bytes = ctypes.c_size_t(0)
     _lib.call("ldb_conv3d_workspace_size", ctypes.byref(desc), ctypes.byref(ws_bytes))

@@ -1376,7 +1376,8 @@ int plan_conv(const ldb_conv_desc* d, ConvPlan* plan) {
   const long long out_tiles =
       static_cast<long long>(B) * p.tiles_d * p.tiles_h * p.tiles_w * p.parities * p.n_tiles;
   if (out_tiles > (1LL << 30)) return fail(LDB_ERR_SHAPE, "conv has too many tiles");
-  const int sms = sm_count();
+  if (d->max_ctas < 0) return fail(LDB_ERR_INVALID, "max_ctas must be >= 0");
+  const int sms = d->max_ctas > 0 ? std::max(2, std::min(sm_count(), d->max_ctas)) : sm_count();
   if (taps == 1 && !exact && bn == 256 && cout % 256 == 0) {
     // Pointwise: K is a few k-blocks, so split-K would only add a reduce
     // pass; fill the SMs with narrower column tiles instead.  Cost per tile

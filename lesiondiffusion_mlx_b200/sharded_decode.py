@@ -199,10 +199,13 @@ class ShardedVqDecoder:
     depth of the whole volume, and returns the output slabs.
     """
 
-    def __init__(self, decoder: VqDecoderB200, comm):
+    def __init__(self, decoder: VqDecoderB200, comm, *, halo_sms: int = 0):
         self.dec = decoder
         self.p = decoder.p
         self.comm = comm
+        # SMs the slab-interior conv leaves free for the halo exchange's
+        # communication kernels, which otherwise wait for it (0: none)
+        self.halo_sms = int(halo_sms)
 
     # ------------------------------------------------------------ primitives
 
@@ -228,11 +231,11 @@ class ShardedVqDecoder:
                 o.stats = torch.zeros((1, packed.out_channels, 2), dtype=torch.float64, device=o.buf.device)
         res = [None] * len(src) if residual is None else [r.x for r in residual]
 
-        def run(s: _Slab, o: _Slab, r, first: int, last: int) -> None:
+        def run(s: _Slab, o: _Slab, r, first: int, last: int, max_ctas: int = 0) -> None:
             """Output slices [first, last) of the slab from input slices [first, last + 2) of its halo buffer."""
             conv3d_ndhwc(s.full[:, first:last + 2], packed, bias, out=o.x[:, up * first:up * last],
                           residual=None if r is None else r[:, up * first:up * last], output_scale=output_scale,
-                          stats=o.stats, depth_halo=1)
+                          stats=o.stats, depth_halo=1, max_ctas=max_ctas)
 
         if not halo:
             for s, o, r in zip(src, out, res):
@@ -241,8 +244,12 @@ class ShardedVqDecoder:
         handle = self.comm.exchange_begin([s.buf for s in src])
         split = all(int(s.x.shape[1]) >= 3 for s in src)
         if split:
+            interior_ctas = 0
+            if self.halo_sms > 0 and handle is not None:
+                sms = torch.cuda.get_device_properties(src[0].buf.device).multi_processor_count
+                interior_ctas = max(2, sms - self.halo_sms)
             for s, o, r in zip(src, out, res):
-                run(s, o, r, 1, int(s.x.shape[1]) - 1)
+                run(s, o, r, 1, int(s.x.shape[1]) - 1, interior_ctas)
         self.comm.exchange_end(handle)
         for s, o, r in zip(src, out, res):
             d = int(s.x.shape[1])

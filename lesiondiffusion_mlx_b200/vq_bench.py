@@ -34,7 +34,7 @@ def _weights(device) -> dict[str, torch.Tensor]:
 
 
 def measure(config: str, device: torch.device, *, steps: int = 3, warmup: int = 1, groups: int = 32,
-            dist=None) -> dict:
+            dist=None, halo_sms: int = 0) -> dict:
     """Time the config-4 decode (``"4a"`` / ``"4b"``) on this rank and return its record.
 
     With ``dist`` (an initialised ``torch.distributed`` with more than one
@@ -57,7 +57,7 @@ def measure(config: str, device: torch.device, *, steps: int = 3, warmup: int = 
 
         start, stop = partition_depth(depth, world)[rank]
         comm = DistDepthComm(timed=True)
-        sharded = ShardedVqDecoder(dec, comm)
+        sharded = ShardedVqDecoder(dec, comm, halo_sms=halo_sms)
 
         def run():
             return sharded.decode([zbuf[:, start:stop]], depth, quantize=False)[0]
@@ -113,6 +113,7 @@ def measure(config: str, device: torch.device, *, steps: int = 3, warmup: int = 
         local = {k: float(np.median([c[k] for c in comm_times])) for k in ("exchange", "all_reduce")}
         t = torch.tensor([local["exchange"], local["all_reduce"]], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        record["halo_sms"] = halo_sms
         record["halo_exchange_ms"] = float(t[0].item())
         record["gn_all_reduce_ms"] = float(t[1].item())
         record["halo_exchanges"] = int(comm_times[0]["exchange_calls"])
@@ -128,6 +129,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--groups", type=int, default=32)
+    ap.add_argument("--halo-sms", type=int, default=0, help="SMs the slab-interior conv leaves to the halo exchange")
     a = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -140,7 +142,8 @@ def main() -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-    record = measure(a.config, device, steps=a.steps, warmup=a.warmup, groups=a.groups, dist=dist)
+    record = measure(a.config, device, steps=a.steps, warmup=a.warmup, groups=a.groups, dist=dist,
+                     halo_sms=a.halo_sms)
     if rank == 0:
         print(json.dumps({"metric": "VQ decode TFLOP/s", **record}), flush=True)
     if dist is not None:

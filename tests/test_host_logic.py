@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.ldb_version() == 2
+    assert lib.ldb_version() == 3
 
 
 def test_errors_are_reported_without_a_device():
@@ -59,7 +59,7 @@ def test_conv_descriptor_of_another_layout_is_rejected():
                          res_ld=8, mode=0, exact=0, out_dtype=0, act=0, output_scale=1.0)
     size = ctypes.c_size_t(0)
     _lib.call("ldb_conv3d_workspace_size", ctypes.byref(good), ctypes.byref(size))
-    assert good.struct_size == ctypes.sizeof(_lib.ConvDesc) == 72
+    assert good.struct_size == ctypes.sizeof(_lib.ConvDesc) == 80
 
     class ShortDesc(ctypes.Structure):
         # the version-1 layout: no struct_size, and it ends at depth_halo
@@ -88,8 +88,12 @@ def test_conv_descriptor_of_another_layout_is_rejected():
             rc = fn(ctypes.cast(buf, ctypes.POINTER(_lib.ConvDesc)), *args)
         assert rc == -1, name  # LDB_ERR_INVALID
         assert b"struct_size" in lib.ldb_last_error(), name
-    good.struct_size = 64
-    with pytest.raises(_lib.LdbError, match="struct_size 64"):
+    good.struct_size = 72  # the version-2 layout (no max_ctas)
+    with pytest.raises(_lib.LdbError, match="struct_size 72"):
+        _lib.call("ldb_conv3d_workspace_size", ctypes.byref(good), ctypes.byref(size))
+    good.struct_size = ctypes.sizeof(_lib.ConvDesc)
+    good.max_ctas = -1
+    with pytest.raises(_lib.LdbError, match="max_ctas"):
         _lib.call("ldb_conv3d_workspace_size", ctypes.byref(good), ctypes.byref(size))
 
 
