@@ -199,12 +199,13 @@ class ShardedVqDecoder:
     depth of the whole volume, and returns the output slabs.
     """
 
-    def __init__(self, decoder: VqDecoderB200, comm, *, halo_sms: int = 0):
+    def __init__(self, decoder: VqDecoderB200, comm, *, halo_sms: int = 8):
         self.dec = decoder
         self.p = decoder.p
         self.comm = comm
-        # SMs the slab-interior conv leaves free for the halo exchange's
-        # communication kernels, which otherwise wait for it (0: none)
+        # SMs the slab-interior conv leaves free, while an exchange is in
+        # flight, for the exchange's communication kernels, which otherwise
+        # wait for the conv's persistent grid to finish (0: none)
         self.halo_sms = int(halo_sms)
 
     # ------------------------------------------------------------ primitives

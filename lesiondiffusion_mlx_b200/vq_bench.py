@@ -34,7 +34,7 @@ def _weights(device) -> dict[str, torch.Tensor]:
 
 
 def measure(config: str, device: torch.device, *, steps: int = 3, warmup: int = 1, groups: int = 32,
-            dist=None, halo_sms: int = 0) -> dict:
+            dist=None, halo_sms: int = 8) -> dict:
     """Time the config-4 decode (``"4a"`` / ``"4b"``) on this rank and return its record.
 
     With ``dist`` (an initialised ``torch.distributed`` with more than one
@@ -129,7 +129,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--groups", type=int, default=32)
-    ap.add_argument("--halo-sms", type=int, default=0, help="SMs the slab-interior conv leaves to the halo exchange")
+    ap.add_argument("--halo-sms", type=int, default=8, help="SMs the slab-interior conv leaves to the halo exchange")
     a = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
