@@ -16,15 +16,20 @@ namespace {
 // [cos, sin] sinusoidal embedding (mlx_model.py:609-612): with h = C/2,
 // freq_i = exp(-ln(1e4) * i / h) and phase = t * freq_i, all in FP32 and in
 // the reference's operation order; out is f16 or f32 (B, C).
-__global__ void timestep_embedding_kernel(const int* table, const int* step, int batch, int channels, void* out,
-                                          int out_f32) {
+__global__ void timestep_embedding_kernel(const int* table, const int* step, int steps, int batch, int channels,
+                                          void* out, int out_f32, unsigned int* status) {
   pdl_begin();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int half = channels / 2;
   if (idx >= batch * half) return;
+  const int row = step ? *step : 0;
+  if (row < 0 || row >= steps) {  // a counter past the table: write nothing, report it
+    if (idx == 0) set_bad_shape(status);
+    return;
+  }
   const int b = idx / half;
   const int i = idx % half;
-  const int* t = table + (step ? static_cast<long long>(*step) * batch : 0);
+  const int* t = table + static_cast<long long>(row) * batch;
   const float scaled = __fmul_rn(-9.21034037197618273607f, static_cast<float>(i));
   // Correctly rounded exp of the FP32 argument: the phase t * freq scales
   // any ulp of freq by t (up to 1000), so freq must not carry expf's error.
@@ -128,6 +133,8 @@ __global__ void dense_small_kernel(const __half* x, int x_ld, const __half* w, c
 struct StepArgs {
   const float* coeff;  // [steps][5] f32 coefficient table (device)
   const int* step;     // current step index (device), or null for step 0
+  int steps;           // rows of the step tables: a step outside [0, steps) touches nothing
+  unsigned int* status;
   long long noise_step_stride;  // elements between the noise of consecutive steps
   float* x;            // (B, V, C) f32 state, updated in place
   float* prev;         // (B, V, C) f32 DPM history
@@ -162,8 +169,12 @@ __global__ void sampler_step_kernel(StepArgs a) {
   const long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (v >= a.voxels) return;
   const int C = a.channels;
-  const float m = a.mask ? a.mask[v] : 1.f;
   const int step = a.step ? *a.step : 0;
+  if (step < 0 || step >= a.steps) {  // a counter past the tables: write nothing, report it
+    if (v == 0) set_bad_shape(a.status);
+    return;
+  }
+  const float m = a.mask ? a.mask[v] : 1.f;
   float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f, k4 = 0.f;
   if (a.kind != 0) {
     const float* k = a.coeff + 5LL * step;
@@ -391,14 +402,18 @@ __global__ void step_advance_kernel(int* step) {
 
 extern "C" {
 
-int ldb_timestep_embedding(cudaStream_t stream, const int* timesteps, const int* step, int batch, int channels,
-                           void* out, int out_dtype) {
+int ldb_timestep_embedding(cudaStream_t stream, const int* timesteps, const int* step, int steps, int batch,
+                           int channels, void* out, int out_dtype) {
   using namespace ldb;
   if (!timesteps || !out) return fail(LDB_ERR_INVALID, "timestep_embedding: null pointer");
   if (batch <= 0 || channels <= 0 || channels % 2) return fail(LDB_ERR_SHAPE, "channels must be even and positive");
+  if (step && steps <= 0) return fail(LDB_ERR_SHAPE, "timestep_embedding: the step table needs >= 1 row");
+  unsigned int* status = device_status_ptr();
+  if (!status) return fail(LDB_ERR_CUDA, "timestep_embedding: no device status word");
   const int n = batch * (channels / 2);
   return launch_kernel(timestep_embedding_kernel, dim3((n + 255) / 256), dim3(256), 0, stream,
-                       "timestep_embedding launch", timesteps, step, batch, channels, out, int(out_dtype == LDB_F32));
+                       "timestep_embedding launch", timesteps, step, step ? steps : 1, batch, channels, out,
+                       int(out_dtype == LDB_F32), status);
 }
 
 int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w, const float* bias, void* out,
@@ -418,9 +433,10 @@ int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w,
 int ldb_sampler_step_ex(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_dtype,
                         int eps_ld, const float* noise, long long noise_step_stride, const float* mask,
                         const float* image, int image_channels, void* net_in, int in_ld, int net_split, int batch,
-                        int voxels, int channels, const float* coeff_table, const int* step) {
+                        int voxels, int channels, const float* coeff_table, const int* step, int steps) {
   using namespace ldb;
   if (kind < 0 || kind > 2) return fail(LDB_ERR_INVALID, "sampler step kind %d", kind);
+  if (step && steps <= 0) return fail(LDB_ERR_SHAPE, "sampler_step: the step tables need >= 1 row");
   if (!x || channels <= 0 || batch <= 0 || voxels <= 0) return fail(LDB_ERR_SHAPE, "sampler_step: bad extents");
   if (kind >= 1 && (!eps || !coeff_table || eps_ld < channels))
     return fail(LDB_ERR_INVALID, "sampler_step: eps/coeff");
@@ -436,6 +452,9 @@ int ldb_sampler_step_ex(cudaStream_t stream, int kind, float* x, float* prev, co
   StepArgs a{};
   a.coeff = coeff_table;
   a.step = step;
+  a.steps = step ? steps : 1;
+  a.status = device_status_ptr();
+  if (!a.status) return fail(LDB_ERR_CUDA, "sampler_step: no device status word");
   a.noise_step_stride = noise_step_stride;
   a.x = x;
   a.prev = prev;
@@ -460,9 +479,9 @@ int ldb_sampler_step_ex(cudaStream_t stream, int kind, float* x, float* prev, co
 int ldb_sampler_step(cudaStream_t stream, int kind, float* x, float* prev, const void* eps, int eps_ld,
                      const float* noise, long long noise_step_stride, const float* mask, const float* image,
                      int image_channels, void* net_in, int in_ld, int batch, int voxels, int channels,
-                     const float* coeff_table, const int* step) {
+                     const float* coeff_table, const int* step, int steps) {
   return ldb_sampler_step_ex(stream, kind, x, prev, eps, LDB_F16, eps_ld, noise, noise_step_stride, mask, image,
-                             image_channels, net_in, in_ld, 0, batch, voxels, channels, coeff_table, step);
+                             image_channels, net_in, in_ld, 0, batch, voxels, channels, coeff_table, step, steps);
 }
 
 int ldb_vq_nearest4(cudaStream_t stream, const void* z, int z_ld, long long positions, const void* codebook,

@@ -166,6 +166,10 @@ def step_case(eager: int, iters: int) -> list[dict]:
     from . import instrument
 
     prepared = _config3_step()
+    # every step below advances the schedule's device step counter: stay inside its tables
+    executed = eager if eager > 0 else iters + 7
+    if executed > prepared.sampler.steps:
+        raise ValueError(f"{executed} steps exceed the {prepared.sampler.steps}-step schedule")
     if eager > 0:
         for _ in range(eager):
             prepared._step()

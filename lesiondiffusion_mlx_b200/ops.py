@@ -249,14 +249,16 @@ def _flash_attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, h
 
 def timestep_embedding(timesteps: torch.Tensor, channels: int, *, step: torch.Tensor | None = None,
                        out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
-    """[cos, sin] embedding of int32 ``timesteps`` ``(B,)`` (or row ``*step`` of a ``(S, B)`` table)."""
+    """[cos, sin] embedding of int32 ``timesteps`` ``(B,)`` (or row ``*step`` of a ``(S, B)`` table;
+    a step outside the table writes nothing and sets the device status, ``ldb_device_status``)."""
     if timesteps.dtype != torch.int32:
         raise ValueError("timesteps must be int32")
     batch = int(timesteps.shape[-1])
+    steps = int(timesteps.numel() // max(batch, 1))
     if out is None:
         out = torch.empty((batch, channels), dtype=out_dtype, device=timesteps.device)
-    _lib.call("ldb_timestep_embedding", _stream(timesteps), timesteps.data_ptr(), _ptr(step), batch, channels,
-              out.data_ptr(), _DT[out.dtype])
+    _lib.call("ldb_timestep_embedding", _stream(timesteps), timesteps.data_ptr(), _ptr(step), steps, batch,
+              channels, out.data_ptr(), _DT[out.dtype])
     return out
 
 
@@ -289,8 +291,15 @@ def sampler_step(
 
     ``eps`` is the f16 or f32 prediction; with ``net_split`` the next network
     input is written in the FP32-exact split format (hi plane, then 2^11-scaled
-    low plane, each padded to 16 channels)."""
+    low plane, each padded to 16 channels).  With ``step`` the coefficient and
+    noise tables are read at ``*step``; a step past either table writes
+    nothing and sets the device status (``ldb_device_status``)."""
     voxels, channels, _ = _rows(x)
+    steps = 2 ** 31 - 1  # rows of the step tables (the smaller of the two)
+    if coeff is not None:
+        steps = min(steps, int(coeff.numel() // 5))
+    if noise is not None and noise_step_stride > 0:
+        steps = min(steps, int(noise.numel() // noise_step_stride))
     batch = int(x.shape[0])
     eps_ld = 0
     if eps is not None:
@@ -306,7 +315,7 @@ def sampler_step(
             "ldb_sampler_step_ex", _stream(x), kind, x.data_ptr(), _ptr(prev), _ptr(eps),
             _DT[eps.dtype] if eps is not None else _lib.LDB_F16, eps_ld, _ptr(noise), int(noise_step_stride),
             _ptr(mask), _ptr(image), image_c, _ptr(net_in), in_ld, int(net_split), batch, voxels, channels,
-            _ptr(coeff), _ptr(step),
+            _ptr(coeff), _ptr(step), steps,
         )
 
 

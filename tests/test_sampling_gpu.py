@@ -71,3 +71,35 @@ def test_host_streamed_steps_match_device_steps(cuda_device, steps):
     torch.cuda.synchronize()
     for i in range(rounds):
         assert torch.equal(host_out[i], want[i].cpu()), f"step {i}"
+
+
+def test_step_counter_past_the_tables_touches_nothing(cuda_device):
+    """A step graph replayed past the end of its schedule: with the device
+    step counter at the tables' row count, the sampler step and the timestep
+    embedding read and write nothing and set status bit 1 instead."""
+    from lesiondiffusion_mlx_b200 import _lib, ops
+
+    _lib.device_status(reset=True)
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    rows, shape = 3, (1, 4, 6, 6, 4)
+    x = torch.randn(shape, generator=g, device=cuda_device)
+    eps = torch.randn(shape, generator=g, device=cuda_device).half()
+    noise = torch.randn((rows, *shape), generator=g, device=cuda_device)
+    coeff = torch.tensor([[0.5, 0.6, 0.1, 0.7, 0.0]] * rows, device=cuda_device)
+    table = torch.arange(2 * rows, dtype=torch.int32, device=cuda_device).view(rows, 2)
+    emb = torch.full((2, 32), 7.0, device=cuda_device)
+    step = torch.tensor([rows - 1], dtype=torch.int32, device=cuda_device)
+    before = x.clone()
+    ops.sampler_step(1, x, eps=eps, noise=noise, noise_step_stride=int(noise[0].numel()), coeff=coeff, step=step)
+    ops.timestep_embedding(table, 32, step=step, out=emb)
+    torch.cuda.synchronize()
+    assert _lib.device_status(reset=False) == 0
+    assert not torch.equal(x, before) and not torch.equal(emb, torch.full_like(emb, 7.0))
+    step.fill_(rows)  # one past the last row
+    moved, emb_before = x.clone(), emb.clone()
+    ops.sampler_step(1, x, eps=eps, noise=noise, noise_step_stride=int(noise[0].numel()), coeff=coeff, step=step)
+    ops.timestep_embedding(table, 32, step=step, out=emb)
+    torch.cuda.synchronize()
+    assert torch.equal(x, moved) and torch.equal(emb, emb_before)
+    assert _lib.device_status(reset=True) & 2
+    assert _lib.device_status(reset=False) == 0
