@@ -63,9 +63,8 @@ enum { LDB_ACT_NONE = 0, LDB_ACT_GELU = 1 };
 
 /* Library ABI version (LDB_ABI_VERSION).  Version 2 added
  * ldb_conv_desc.struct_size as the descriptor's first field, version 3
- * ldb_conv_desc.max_ctas, version 4 ldb_conv3d_fwd_rows, ldb_row_norm and the
- * step-table row count (`steps`) of ldb_timestep_embedding and
- * ldb_sampler_step[_ex]. */
+ * ldb_conv_desc.max_ctas, version 4 the step-table row count (`steps`) of
+ * ldb_timestep_embedding and ldb_sampler_step[_ex]. */
 LDB_API int ldb_version(void);
 
 /* Number of kernels this library has launched (or recorded into a CUDA
@@ -162,43 +161,6 @@ LDB_API int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_pari
 LDB_API int ldb_conv3d_fwd(ldb_stream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
                    const float* bias, const float* shift, const void* residual, void* out, void* workspace,
                    size_t workspace_bytes);
-
-/* Token LayerNorm folded into the dense layers around it.  The reference's
- * transformer block runs LayerNorm -> dense three times
- * (lesiondiffusion_mlx/mlx_model.py:522-552, layer_norm :360-367, dense
- * :204-220); here the dense layer that writes a LayerNorm's input records
- * each row's sums (sums_out) and the dense layer that reads the normalized
- * rows takes the raw rows instead (sums_in):
- *
- *   LN(x) . W + b = rstd * (x . W' - mean * col_sums) + b'
- *
- * with W' = W scaled per input channel by LayerNorm's gamma, b' = b + beta . W
- * and col_sums[o] = sum over input channels of W'[o] as packed (f16).  The
- * row statistics are mean = S1 / in_channels, var = S2 / in_channels - mean^2
- * and rstd = 1 / sqrt(var + eps), from FP64 sums of the f16 values the
- * producer stored.  The reference rounds the normalized rows to f16 before
- * the dense layer; the folded form rounds W' instead, an error of the same
- * size. */
-typedef struct {
-  int struct_size; /* sizeof(ldb_row_norm) as the caller compiled it */
-  /* Per output voxel (token row) r, the FP64 sum and sum of squares of the
-   * row's stored outputs over all out_channels are added to sums_out[2r] and
-   * sums_out[2r + 1] (zero them before the call).  May be null. */
-  double* sums_out;
-  /* The sums of the input rows over in_channels, as a producer call recorded
-   * them: the conv then computes the folded LayerNorm -> dense above with
-   * the caller's W' (packed) and b' (bias).  May be null. */
-  const double* sums_in;
-  const float* col_sums; /* [out_channels], required with sums_in */
-  float eps;             /* LayerNorm epsilon (1e-5 in the reference's transformer) */
-} ldb_row_norm;
-
-/* ldb_conv3d_fwd for an f16 pointwise conv (LDB_CONV_1X1, depth_halo 0) with
- * the row sums and / or the folded LayerNorm of `rows`.  Rows are the output
- * voxels in NDHW order, which for token rows (B, L, C) is b * L + l. */
-LDB_API int ldb_conv3d_fwd_rows(ldb_stream_t stream, const ldb_conv_desc* desc, const void* x,
-                                const void* w_packed, const float* bias, const float* shift, const void* residual,
-                                void* out, const ldb_row_norm* rows, void* workspace, size_t workspace_bytes);
 
 /* -------------------------------------------------------------------------
  * Group normalization: replaces medmlx-core's group_norm_affine (called at

@@ -57,22 +57,6 @@ class ConvDesc(ctypes.Structure):
         self.struct_size = ctypes.sizeof(ConvDesc)
 
 
-class RowNorm(ctypes.Structure):
-    """Mirror of ``ldb_row_norm``; ``struct_size`` is filled in on construction."""
-
-    _fields_ = [
-        ("struct_size", ctypes.c_int),
-        ("sums_out", ctypes.c_void_p),
-        ("sums_in", ctypes.c_void_p),
-        ("col_sums", ctypes.c_void_p),
-        ("eps", ctypes.c_float),
-    ]
-
-    def __init__(self, *args, **kwargs):
-        super().__init__(*args, **kwargs)
-        self.struct_size = ctypes.sizeof(RowNorm)
-
-
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
@@ -89,7 +73,6 @@ SIGNATURES: dict[str, list] = {
     "ldb_conv3d_weight_rows": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_I), ctypes.POINTER(_I)],
     "ldb_conv3d_fwd": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _SZ],
     "ldb_conv3d_fwd_gn_stats": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, _P, _P, _SZ],
-    "ldb_conv3d_fwd_rows": [_P, ctypes.POINTER(ConvDesc), _P, _P, _P, _P, _P, _P, ctypes.POINTER(RowNorm), _P, _SZ],
     "ldb_group_norm_workspace_size": [_I, _I, _I, ctypes.POINTER(_SZ)],
     "ldb_group_norm_affine": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _SZ],
     "ldb_group_norm_affine_noalloc": [_P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P],

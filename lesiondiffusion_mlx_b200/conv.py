@@ -111,30 +111,6 @@ def pack_dense_weight(weight: torch.Tensor) -> PackedWeight:
     return pack_weight(weight[:, :, None, None, None])
 
 
-def fold_layer_norm(weight: torch.Tensor, bias: torch.Tensor | None, gamma: torch.Tensor,
-                    beta: torch.Tensor) -> tuple[PackedWeight, torch.Tensor, torch.Tensor]:
-    """Fold a LayerNorm's affine into the f16 dense layer that reads it.
-
-    ``weight`` ``(O, C)`` and ``bias`` ``(O,)`` (both as the layer holds them,
-    f16 values), ``gamma`` / ``beta`` ``(C,)``.  Returns the packed
-    ``W' = W * gamma`` (rounded to f16 once), the f32 bias ``b + W . beta``
-    (FP64) and the f32 column sums of W' as packed, for ``conv3d_ndhwc``'s
-    ``row_sums_in`` form: ``rstd * (x . W' - mean * colsum) + b'`` equals
-    ``LayerNorm(x) . W + b`` (mlx_model.py:360-367 then :204-220).
-    """
-    if weight.ndim != 2:
-        raise ValueError(f"expected an (O, C) weight, got {tuple(weight.shape)}")
-    w = weight.detach().to(torch.float64)
-    g = gamma.detach().to(w.device, torch.float64)
-    bt = beta.detach().to(w.device, torch.float64)
-    folded = (w * g[None, :]).to(torch.float16)
-    b = torch.zeros(w.shape[0], dtype=torch.float64, device=w.device) if bias is None else \
-        bias.detach().to(w.device, torch.float64)
-    b = (b + w @ bt).to(torch.float32).contiguous()
-    colsum = folded.to(torch.float64).sum(dim=1).to(torch.float32).contiguous()
-    return pack_weight(folded[:, :, None, None, None]), b, colsum
-
-
 def pack_upsample_weight(weight: torch.Tensor) -> PackedWeight:
     """Fold a ``(O, C, 3, 3, 3)`` weight into eight 2x2x2 parity filters.
 
@@ -241,10 +217,6 @@ def conv3d_ndhwc(
     depth_halo: int = 0,
     pad01: bool = False,
     max_ctas: int = 0,
-    row_sums_out: torch.Tensor | None = None,
-    row_sums_in: torch.Tensor | None = None,
-    col_sums: torch.Tensor | None = None,
-    row_eps: float = 1e-5,
 ) -> torch.Tensor:
     """Convolve NDHWC ``x`` ``(B, D, H, W, C)`` (channel stride = ``x.stride(3)``).
 
@@ -258,15 +230,6 @@ def conv3d_ndhwc(
     statistics that ``ops.group_norm_affine_from_stats`` consumes.  With
     ``depth_halo`` = 1, x's first and last depth slices are a neighbour's
     slices (depth-sharded volumes) and the output covers the interior.
-
-    Token LayerNorm folded into pointwise convs (``ldb_conv3d_fwd_rows``):
-    with ``row_sums_out`` (float64 ``(rows, 2)``, zero on entry; rows = the
-    output voxels) the kernel adds each row's sum and sum of squares of its
-    stored values; with ``row_sums_in`` (such sums of x's rows) and
-    ``col_sums`` (f32 ``(O,)``) it computes ``rstd * (x . w - mean * col_sums)
-    + bias``, the dense layer of LayerNorm(x) (epsilon ``row_eps``) when
-    ``packed`` holds the weight scaled by LayerNorm's gamma and ``bias``
-    includes beta's contribution (``fold_layer_norm``).
     """
     if x.device.type != "cuda":
         raise ValueError("conv3d_ndhwc needs CUDA tensors")
@@ -313,29 +276,10 @@ def conv3d_ndhwc(
     if stats is not None and (stats.dtype != torch.float64 or tuple(stats.shape) != (batch, cout, 2)
                               or not stats.is_contiguous()):
         raise ValueError(f"stats must be a contiguous float64 {(batch, cout, 2)} tensor")
-    rows = None
-    if row_sums_out is not None or row_sums_in is not None:
-        if mode != MODE_POINTWISE or packed.exact or depth_halo or stats is not None:
-            raise ValueError("row sums need an f16 pointwise conv without a depth halo or GroupNorm statistics")
-        n_rows = batch * grid[0] * grid[1] * grid[2]
-        for name, t in (("row_sums_out", row_sums_out), ("row_sums_in", row_sums_in)):
-            if t is not None and (t.dtype != torch.float64 or tuple(t.shape) != (n_rows, 2) or not t.is_contiguous()):
-                raise ValueError(f"{name} must be a contiguous float64 {(n_rows, 2)} tensor")
-        if row_sums_in is not None and (col_sums is None or col_sums.dtype != torch.float32
-                                        or tuple(col_sums.shape) != (cout,) or not col_sums.is_contiguous()):
-            raise ValueError("row_sums_in needs contiguous float32 (O,) col_sums")
-        rows = _lib.RowNorm(sums_out=_ptr(row_sums_out), sums_in=_ptr(row_sums_in),
-                            col_sums=_ptr(col_sums) if row_sums_in is not None else None, eps=float(row_eps))
     label = f"mode{mode} B{batch} {grid[0]}x{grid[1]}x{grid[2]} {cin}->{cout}{' exact' if packed.exact else ''}"
     desc.clock = instrument.device_clock("conv3d", flops, x.device, label)
     with instrument.maybe_time("conv3d", flops, device_clocked=desc.clock is not None):
-        if rows is not None:
-            _lib.call(
-                "ldb_conv3d_fwd_rows", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(),
-                _ptr(bias), _ptr(shift), _ptr(residual), out.data_ptr(), ctypes.byref(rows), _ptr(workspace),
-                ws_bytes.value,
-            )
-        elif stats is None:
+        if stats is None:
             _lib.call(
                 "ldb_conv3d_fwd", stream, ctypes.byref(desc), x.data_ptr(), packed.tensor.data_ptr(), _ptr(bias),
                 _ptr(shift), _ptr(residual), out.data_ptr(), _ptr(workspace), ws_bytes.value,

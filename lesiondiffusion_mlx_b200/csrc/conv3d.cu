@@ -257,8 +257,6 @@ struct EpiState {
   float* bsum;           // [BN]
   uint32_t* vmask;       // [2][4] valid-row bits of the current tile (double-buffered by tile)
   float* sacc;           // [BN][2] sums of (x - bsum) and (x - bsum)^2 over the current run of tiles
-  float* csum;           // [BN] weight column sums of a folded LayerNorm (aliases sacc: such a conv
-                         // accumulates no GroupNorm statistics)
   int key_b = -1;        // (batch, column tile) of the run: tiles of one run share bsum
   int key_nt = -1;
   int run_rows = 0;      // valid rows (voxels) accumulated in the run
@@ -411,57 +409,19 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
     const unsigned int valid = __ballot_sync(0xffffffffu, row_voxel(p, c, st.row) >= 0);
     if ((st.row & 31) == 0) vmask[st.quarter] = valid;
   }
-  // The tile's per-column inputs, read while the MMAs still run: bias +
-  // shift (the previous run's statistics were flushed above with its own
-  // values) and, for a folded token LayerNorm (f16 pointwise convs), the
-  // weight column sums and this thread's row factors a = rstd, b = -rstd *
-  // mean, so that a * acc + b * col_sum = rstd * (x - mean) . w.  Every
-  // global load is issued before the shared-memory stores: through generic
-  // pointers a load after a store waits for it, which would put one L2 round
-  // trip per load on the tile's critical path.
-  float ln_a = 1.f, ln_b = 0.f;
-  if constexpr (!SPLIT) {
-    constexpr int kPer = (BN + 127) / 128;
-    const bool fold = !EXACT && p.row_in != nullptr;
-    float add[kPer], cs[kPer];
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int j = et + u * 128;
+  // bias + shift of the tile's columns, read while the MMAs still run (the
+  // previous run's statistics were flushed above with its own values)
+  if (!SPLIT) {
+    for (int j = et; j < BN; j += 128) {
       const int col = n0 + j;
-      add[u] = 0.f;
-      cs[u] = 0.f;
-      if (j < BN && col < p.cout && real) {
-        if (p.bias) add[u] = p.bias[col];
-        if (p.shift) add[u] += p.shift[static_cast<long long>(c.b) * p.cout + col];
-        if (fold) cs[u] = p.col_sums[col];
+      float add = 0.f;
+      if (col < p.cout && real) {
+        if (p.bias) add = p.bias[col];
+        if (p.shift) add += p.shift[static_cast<long long>(c.b) * p.cout + col];
       }
-    }
-    double s1 = 0.0, s2 = 0.0;
-    const long long vox = fold && real ? row_voxel(p, c, st.row) : -1;
-    if (vox >= 0) {
-      s1 = p.row_in[2 * vox];
-      s2 = p.row_in[2 * vox + 1];
-    }
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int j = et + u * 128;
-      if (j < BN) {
-        st.bsum[j] = add[u];
-        if (fold) st.csum[j] = cs[u];
-      }
-    }
-    if (vox >= 0) {
-      // mean and variance from the FP64 sums (no cancellation), then the
-      // FP32 1 / sqrt(var + eps) of the reference's FP32 LayerNorm
-      const double mean = s1 * p.row_inv_n;
-      const double var = fmax(fma(-mean, mean, s2 * p.row_inv_n), 0.0);
-      ln_a = 1.0f / sqrtf(static_cast<float>(var) + p.row_eps);
-      ln_b = -ln_a * static_cast<float>(mean);
+      st.bsum[j] = add;
     }
   }
-  // This thread's row sums of the stored values over the tile's columns
-  // (producer of a folded LayerNorm; at most 256 f16 values per tile, FP32).
-  float row_s1 = 0.f, row_s2 = 0.f;
   bool ok = warp_wait(acc_full_bar, acc_parity, st.abort_flag, st.status);
   tc_fence_after();
   named_barrier(1, 128);
@@ -527,16 +487,10 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
         st.rq += 1;
         rbuf = res_base + rb * Cfg::kEpiBufBytes;
       }
-      // Every shared-memory read of the chunk (column sums, bias + shift, the
-      // residual) comes before its first staging store: the compiler cannot
-      // tell the staging buffer from those arrays, and loads interleaved with
-      // stores would run one after another.
-      if constexpr (!EXACT) {
-        if (p.row_in) {
-#pragma unroll
-          for (int j = 0; j < CC; ++j) v[j] = fmaf(ln_a, v[j], ln_b * st.csum[c0 + j]);
-        }
-      }
+      // Every shared-memory read of the chunk (bias + shift, the residual)
+      // comes before its first staging store: the compiler cannot tell the
+      // staging buffer from those arrays, and loads interleaved with stores
+      // would run one after another.
 #pragma unroll
       for (int j = 0; j < CC; ++j) v[j] = (v[j] + st.bsum[c0 + j]) * p.out_scale;
       if (rbuf) {
@@ -570,7 +524,6 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
           v[j] = gelu_erf_f32(z);
         }
       }
-      float cs1 = 0.f, cs2 = 0.f;  // the chunk's row sums of the stored (rounded) values
 #pragma unroll
       for (int u = 0; u < CC / kPerUnit; ++u) {
         const uint32_t off = swizzle_offset(rowoff + u * 16, kRowBytes);
@@ -582,21 +535,6 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
 #pragma unroll
           for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(v[8 * u + 2 * j], v[8 * u + 2 * j + 1]);
           *reinterpret_cast<uint4*>(ob + off) = raw;
-          if (p.row_out) {
-            // columns past cout are exact zeros (zero weight rows, no bias, zero-filled residual)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __half22float2(h2[j]);
-              cs1 += f.x + f.y;
-              cs2 = fmaf(f.x, f.x, fmaf(f.y, f.y, cs2));
-            }
-          }
-        }
-      }
-      if constexpr (!EXACT) {
-        if (p.row_out) {
-          row_s1 += cs1;
-          row_s2 += cs2;
         }
       }
     }
@@ -615,15 +553,6 @@ __device__ __forceinline__ bool epilogue_tile(const ConvParams& p, const ConvMap
       if (p.stats) chunk_stats<CC, kElem>(p, n0, c0, ob, vmask, st.bsum, st.sacc);
     }
     st.oq += 1;
-  }
-  if constexpr (!SPLIT && !EXACT) {
-    if (p.row_out && real) {
-      const long long vox = row_voxel(p, c, st.row);
-      if (vox >= 0) {
-        red_add_f64(p.row_out + 2 * vox, static_cast<double>(row_s1));
-        red_add_f64(p.row_out + 2 * vox + 1, static_cast<double>(row_s2));
-      }
-    }
   }
   return ok;
 }
@@ -1098,7 +1027,6 @@ __global__ void __launch_bounds__(ConvCfg<KC, BN, EXACT, TRANS, PAIR>::kThreads,
     st.bsum = bsum;
     st.vmask = vmask;
     st.sacc = sacc;
-    st.csum = sacc;
     st.abort_flag = abort_flag;
     st.status = status;
     st.quarter = warp & 3;
@@ -1578,7 +1506,7 @@ int ldb_conv3d_weight_rows(const ldb_conv_desc* desc, int* rows_per_parity, int*
 
 static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
                         const float* bias, const float* shift, const void* residual, void* out, double* stats,
-                        const ldb_row_norm* rows, void* workspace, size_t workspace_bytes) {
+                        void* workspace, size_t workspace_bytes) {
   using namespace ldb;
   ldb_conv_desc flat;
   desc = flat_pointwise(desc, &flat);
@@ -1599,13 +1527,6 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
   p.residual = residual;
   p.out = out;
   p.stats = stats;
-  if (rows) {
-    p.row_out = rows->sums_out;
-    p.row_in = rows->sums_in;
-    p.col_sums = rows->col_sums;
-    p.row_inv_n = 1.0 / static_cast<double>(desc->in_channels);
-    p.row_eps = rows->eps;
-  }
   p.clock = desc->clock;
   p.partials = static_cast<float*>(workspace);
 
@@ -1730,35 +1651,14 @@ static int conv_forward(cudaStream_t stream, const ldb_conv_desc* desc, const vo
 int ldb_conv3d_fwd(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
                    const float* bias, const float* shift, const void* residual, void* out, void* workspace,
                    size_t workspace_bytes) {
-  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, nullptr, nullptr, workspace,
-                      workspace_bytes);
+  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, nullptr, workspace, workspace_bytes);
 }
 
 int ldb_conv3d_fwd_gn_stats(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
                             const float* bias, const float* shift, const void* residual, void* out, double* stats,
                             void* workspace, size_t workspace_bytes) {
   if (!stats) return ldb::fail(LDB_ERR_INVALID, "conv3d: stats is null");
-  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, stats, nullptr, workspace,
-                      workspace_bytes);
-}
-
-int ldb_conv3d_fwd_rows(cudaStream_t stream, const ldb_conv_desc* desc, const void* x, const void* w_packed,
-                        const float* bias, const float* shift, const void* residual, void* out,
-                        const ldb_row_norm* rows, void* workspace, size_t workspace_bytes) {
-  using ldb::fail;
-  if (!rows) return fail(LDB_ERR_INVALID, "conv3d rows: row_norm is null");
-  if (rows->struct_size != static_cast<int>(sizeof(ldb_row_norm)))
-    return fail(LDB_ERR_INVALID, "row_norm struct_size %d != %d (ABI version %d)", rows->struct_size,
-                static_cast<int>(sizeof(ldb_row_norm)), LDB_ABI_VERSION);
-  if (!desc) return fail(LDB_ERR_INVALID, "conv descriptor is null");
-  if (desc->struct_size == static_cast<int>(sizeof(ldb_conv_desc)) &&
-      (desc->mode != LDB_CONV_1X1 || desc->exact != 0 || desc->depth_halo != 0))
-    return fail(LDB_ERR_INVALID, "row sums and the folded LayerNorm need an f16 pointwise conv without a depth halo");
-  if (!rows->sums_out && !rows->sums_in) return fail(LDB_ERR_INVALID, "row_norm has neither sums_out nor sums_in");
-  if (rows->sums_in && !rows->col_sums) return fail(LDB_ERR_INVALID, "row_norm: sums_in needs col_sums");
-  if (rows->sums_in && !(rows->eps >= 0.f)) return fail(LDB_ERR_INVALID, "row_norm: eps must be >= 0");
-  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, nullptr, rows, workspace,
-                      workspace_bytes);
+  return conv_forward(stream, desc, x, w_packed, bias, shift, residual, out, stats, workspace, workspace_bytes);
 }
 
 }  // extern "C"

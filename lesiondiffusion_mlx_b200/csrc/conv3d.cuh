@@ -67,17 +67,6 @@ struct ConvParams {
   // GroupNorm statistics of the stored output (may be null): per (batch,
   // channel) the FP64 sum and sum of squares, added atomically.
   double* stats;
-  // Token LayerNorm folded into pointwise convs (f16 voxel-major tiles only;
-  // may be null).  row_out: per output voxel the FP64 sum and sum of squares
-  // of its stored values over all columns, added atomically.  row_in: the
-  // same sums of the input rows; the epilogue then computes
-  // rstd * (acc - mean * col_sums[o]) before the bias (mean = S1 * row_inv_n,
-  // var = S2 * row_inv_n - mean^2, rstd = 1 / sqrt(var + row_eps)).
-  double* row_out;
-  const double* row_in;
-  const float* col_sums;
-  double row_inv_n;
-  float row_eps;
   int out_d, out_h, out_w;
   // Device-clock timing of the launch (may be null): [start, end] in ns.
   unsigned long long* clock;

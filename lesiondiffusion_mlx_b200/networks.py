@@ -27,7 +27,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib, ops
-from .conv import PackedWeight, conv3d_ndhwc, fold_layer_norm, pack_upsample_weight, pack_weight
+from .conv import PackedWeight, conv3d_ndhwc, pack_upsample_weight, pack_weight
 
 UPSAMPLE_CONV = re.compile(r"(?:^output_blocks\.\d+\.\d+|\.upsample)\.conv$")
 
@@ -104,18 +104,6 @@ class _Params:
 
         return self._get("dbias", "|".join(keys), build)
 
-    def dense_folded(self, keys: tuple[str, ...], norm_key: str) -> tuple[PackedWeight, torch.Tensor, torch.Tensor]:
-        """The dense layer(s) ``keys`` with LayerNorm ``norm_key``'s affine folded in
-        (``conv.fold_layer_norm``): packed weight, bias, weight column sums."""
-
-        def build():
-            ws = [self.raw[k + ".weight"] for k in keys]
-            w = torch.cat([t.reshape(t.shape[0], -1) for t in ws], 0).to(self.device, self.dtype)
-            return fold_layer_norm(w, self.dense_bias(*keys), self.f32(norm_key + ".weight"),
-                                   self.f32(norm_key + ".bias"))
-
-        return self._get("dense_ln", "|".join(keys) + "@" + norm_key, build)
-
 
 def _voxels(x: torch.Tensor) -> tuple[int, int, int]:
     return int(x.shape[1]), int(x.shape[2]), int(x.shape[3])
@@ -145,63 +133,43 @@ class _Layers:
         # statistics slices from: allocated once per (batch, device) and
         # cleared by a memset at the start of every forward (a memset node in
         # a captured step, no kernel).
-        # The arena's tail holds the token-row sums of the folded LayerNorms
-        # (``rows`` rows of (sum, sum of squares)), cleared by the same memset.
         self._arena: torch.Tensor | None = None
-        self._arenas: dict[tuple[int, int, torch.device], torch.Tensor] = {}
+        self._arenas: dict[tuple[int, torch.device], torch.Tensor] = {}
         self._arena_pos = 0
-        self._rows_pos = 0
-        self._rows_end = 0
         self._stats_channels = sum(int(w.shape[0]) for w in params.raw.values() if w.ndim == 5)
 
-    def _begin_stats(self, batch: int, device: torch.device, rows: int = 0) -> None:
-        key = (batch, rows, device)
+    def _begin_stats(self, batch: int, device: torch.device) -> None:
+        key = (batch, device)
         arena = self._arenas.get(key)
         if arena is None:
-            arena = torch.empty(batch * self._stats_channels * 2 + rows * 2, dtype=torch.float64, device=device)
+            arena = torch.empty(batch * self._stats_channels * 2, dtype=torch.float64, device=device)
             self._arenas[key] = arena
         _lib.call("ldb_clear_async", torch.cuda.current_stream(device).cuda_stream, arena.data_ptr(),
                   arena.numel() * arena.element_size())
         self._arena = arena
         self._arena_pos = 0
-        self._rows_pos = batch * self._stats_channels * 2
-        self._rows_end = arena.numel()
 
     def _take_stats(self, batch: int, channels: int) -> torch.Tensor | None:
         n = batch * channels * 2
-        if self._arena is None or self._arena_pos + n > self._rows_pos:
+        if self._arena is None or self._arena_pos + n > self._arena.numel():
             return None
         t = self._arena[self._arena_pos : self._arena_pos + n].view(batch, channels, 2)
         self._arena_pos += n
         return t
 
-    def _take_rows(self, rows: int, count: int) -> list[torch.Tensor] | None:
-        """``count`` zeroed float64 (rows, 2) row-sum buffers, or None when the
-        arena has no room for all of them."""
-        n = rows * 2
-        if self._arena is None or self._rows_pos + count * n > self._rows_end:
-            return None
-        out = []
-        for _ in range(count):
-            out.append(self._arena[self._rows_pos : self._rows_pos + n].view(rows, 2))
-            self._rows_pos += n
-        return out
-
     def conv(self, x: torch.Tensor, key: str, *, stride: int = 1, residual: torch.Tensor | None = None,
              shift: torch.Tensor | None = None, output_scale: float = 1.0, stats: bool = False,
-             pad01: bool = False, row_sums: torch.Tensor | None = None) -> torch.Tensor:
+             pad01: bool = False) -> torch.Tensor:
         """3x3x3 (stride 1/2, or folded up-2x) or pointwise conv of NDHWC f16 x.
 
         With ``stats`` the output also carries its GroupNorm statistics,
         accumulated by the conv epilogue, for the GroupNorm that reads it;
-        ``pad01`` pads a stride-2 conv with zeros only after each axis;
-        ``row_sums`` receives the output rows' sums for a folded LayerNorm."""
+        ``pad01`` pads a stride-2 conv with zeros only after each axis."""
         packed = self.p.conv(key, stride)
         st = self._take_stats(int(x.shape[0]), packed.out_channels) if stats else None
         x, cin = self._conv_input(x)
         out = conv3d_ndhwc(x, packed, self.p.f32(key + ".bias"), stride=stride, residual=residual, shift=shift,
-                           output_scale=output_scale, stats=st, pad01=pad01, in_channels=cin,
-                           row_sums_out=row_sums)
+                           output_scale=output_scale, stats=st, pad01=pad01, in_channels=cin)
         if st is not None:
             setattr(out, _GN_STATS, st)
         return out
@@ -244,26 +212,15 @@ class _Layers:
         return self.conv(prepared, conv_key, residual=residual, shift=shift, output_scale=output_scale, stats=stats)
 
     def dense(self, x: torch.Tensor, *keys: str, residual: torch.Tensor | None = None,
-              act: int = _lib.LDB_ACT_NONE, norm: tuple[str, torch.Tensor] | None = None,
-              sums_out: torch.Tensor | None = None) -> torch.Tensor:
-        """Linear layer(s) on token rows (B, L, C) via the pointwise tensor-core conv.
-
-        ``norm`` = (LayerNorm key, row sums of x): the layer reads LayerNorm(x)
-        with the LayerNorm folded into it (f16 only); ``sums_out`` receives the
-        output rows' sums for the next folded LayerNorm."""
-        colsum = sums_in = None
-        if norm is not None:
-            packed, bias, colsum = self.p.dense_folded(keys, norm[0])
-            sums_in = norm[1]
-        else:
-            packed = self.p.dense_packed(*keys)
-            bias = self.p.dense_bias(*keys)
+              act: int = _lib.LDB_ACT_NONE) -> torch.Tensor:
+        """Linear layer(s) on token rows (B, L, C) via the pointwise tensor-core conv."""
+        packed = self.p.dense_packed(*keys)
+        bias = self.p.dense_bias(*keys)
         x, cin = self._conv_input(x)
         b, length = int(x.shape[0]), int(x.shape[1])
         x5 = x.unsqueeze(1).unsqueeze(1)
         res5 = None if residual is None else residual.unsqueeze(1).unsqueeze(1)
-        out = conv3d_ndhwc(x5, packed, bias, residual=res5, act=act, in_channels=cin, row_sums_out=sums_out,
-                           row_sums_in=sums_in, col_sums=colsum, row_eps=1e-5)
+        out = conv3d_ndhwc(x5, packed, bias, residual=res5, act=act, in_channels=cin)
         return out.view(b, length, packed.out_channels)
 
 
@@ -324,22 +281,6 @@ class LdmUnetB200(_Layers):
                 self.p.f32(name)
                 self.p.f32(name[: -len("weight")] + "bias")
 
-    def _layer_norm_rows(self, batch: int, grid: tuple[int, int, int]) -> int:
-        """Token rows of all folded LayerNorms of one f16 forward: three per
-        transformer block, at the grid of the block's level (the topology of
-        ``forward``; stride-2 downsampling halves each extent rounding up)."""
-        if self.exact:
-            return 0
-        cfg = self.config
-        total, resolution = 0, 1
-        for level in range(len(cfg.channel_mult)):
-            if resolution in cfg.attention_resolutions:
-                total += (2 * cfg.num_res_blocks + 1) * 3 * batch * grid[0] * grid[1] * grid[2]
-            if level < len(cfg.channel_mult) - 1:
-                grid = tuple((n - 1) // 2 + 1 for n in grid)
-                resolution *= 2
-        return total + 3 * batch * grid[0] * grid[1] * grid[2]  # the middle block
-
     def _pack_dense(self) -> None:
         """Pack the dense layers the forward pass uses (fused Q/K/V, Q alone when
         a context gives K/V, the output and feed-forward projections, the time
@@ -358,13 +299,6 @@ class LdmUnetB200(_Layers):
             for attn in (blk + ".attn1", blk + ".attn2"):
                 groups += [(attn + ".to_q", attn + ".to_k", attn + ".to_v"), (attn + ".to_q",), (attn + ".to_out.0",)]
             groups += [(blk + ".ff.net.0.0",), (blk + ".ff.net.2",)]
-            if not self.exact:  # the folded LayerNorm forms the f16 transformer uses
-                self.p.dense_folded((blk + ".attn1.to_q", blk + ".attn1.to_k", blk + ".attn1.to_v"), blk + ".norm1")
-                for keys, norm in (((blk + ".attn2.to_q",), ".norm2"), ((blk + ".ff.net.0.0",), ".norm3")):
-                    self.p.dense_folded(keys, blk + norm)
-                if self.p.raw[blk + ".attn2.to_k.weight"].shape[1:] == self.p.raw[blk + ".attn2.to_q.weight"].shape[1:]:
-                    qkv2 = tuple(blk + ".attn2.to_" + n for n in "qkv")  # attn2 without a context attends to itself
-                    self.p.dense_folded(qkv2, blk + ".norm2")
         for keys in groups:
             if not keys or not all(k + ".weight" in self.p.raw for k in keys):
                 continue
@@ -474,44 +408,28 @@ class LdmUnetB200(_Layers):
                                    residual=skip, stats=True)
 
     def attention(self, x: torch.Tensor, key: str, heads: int, kv: tuple[torch.Tensor, torch.Tensor] | None,
-                  residual: torch.Tensor, norm: tuple[str, torch.Tensor] | None = None,
-                  sums_out: torch.Tensor | None = None) -> torch.Tensor:
-        """``residual + to_out(attention(x, context))`` (mlx_model.py:443-493); with
-        ``norm`` x is the un-normalized residual stream and the LayerNorm is
-        folded into the Q / K / V projection (``dense``)."""
+                  residual: torch.Tensor) -> torch.Tensor:
+        """``residual + to_out(attention(x, context))`` (mlx_model.py:443-493)."""
         c = getattr(x, _SPLIT_C, None) or int(x.shape[-1])
         if kv is None:
-            qkv = self.dense(x, key + ".to_q", key + ".to_k", key + ".to_v", norm=norm)
+            qkv = self.dense(x, key + ".to_q", key + ".to_k", key + ".to_v")
             q, k, v = qkv[..., :c], qkv[..., c : 2 * c], qkv[..., 2 * c :]
         else:
-            q = self.dense(x, key + ".to_q", norm=norm)
+            q = self.dense(x, key + ".to_q")
             k, v = kv
         depth = c // heads
         attn = ops.flash_attention(q, k, v, heads=heads, scale=depth ** -0.5)
-        return self.dense(attn, key + ".to_out.0", residual=residual, sums_out=sums_out)
+        return self.dense(attn, key + ".to_out.0", residual=residual)
 
     def transformer(self, x: torch.Tensor, key: str, cache: dict) -> torch.Tensor:
         """mlx_model.py:522-552 on NDHWC tokens."""
         b = int(x.shape[0])
         c = int(x.shape[-1])
         normed = self.group_norm_input(x, key + ".norm", groups=32, eps=1e-6, silu=False)
-        heads = c // self.config.num_head_channels
-        blk = key + ".transformer_blocks.0"
-        sums = None if self.exact else self._take_rows(int(x.numel() // x.shape[-1]), 3)
-        if sums is not None:
-            # The three LayerNorms folded into the dense layers that read them;
-            # the layer writing each LayerNorm's input records its row sums.
-            t = self.conv(normed, key + ".proj_in", row_sums=sums[0])
-            tokens = t.view(b, -1, c)
-            tokens = self.attention(tokens, blk + ".attn1", heads, None, tokens, norm=(blk + ".norm1", sums[0]),
-                                    sums_out=sums[1])
-            tokens = self.attention(tokens, blk + ".attn2", heads, cache.get(blk + ".attn2"), tokens,
-                                    norm=(blk + ".norm2", sums[1]), sums_out=sums[2])
-            ff = self.dense(tokens, blk + ".ff.net.0.0", act=_lib.LDB_ACT_GELU, norm=(blk + ".norm3", sums[2]))
-            tokens = self.dense(ff, blk + ".ff.net.2", residual=tokens)
-            return self.conv(tokens.view(t.shape), key + ".proj_out", residual=x, stats=True)
         t = self.conv(normed, key + ".proj_in")
         tokens = t.view(b, -1, c)
+        heads = c // self.config.num_head_channels
+        blk = key + ".transformer_blocks.0"
 
         def ln(t_: torch.Tensor, n: str) -> torch.Tensor:
             out = ops.layer_norm(t_, self.p.f32(f"{blk}.{n}.weight"), self.p.f32(f"{blk}.{n}.bias"), 1e-5,
@@ -550,7 +468,7 @@ class LdmUnetB200(_Layers):
         """Noise prediction for NDHWC f16 ``x`` (B, D, H, W, C_in) (mlx_model.py:599-654)."""
         cfg = self.config
         emb = self.block_shifts(self.time_embedding(timesteps, step))
-        self._begin_stats(int(x.shape[0]), x.device, rows=self._layer_norm_rows(int(x.shape[0]), _voxels(x)))
+        self._begin_stats(int(x.shape[0]), x.device)
         h = self.conv(x, "input_blocks.0.0", stats=True)
         skips = [h]
         block, resolution = 1, 1

@@ -392,57 +392,3 @@ def test_device_status_clean(cuda_device):
     from lesiondiffusion_mlx_b200 import _lib
 
     assert _lib.device_status(reset=True) == 0
-
-
-@pytest.mark.parametrize("tokens,channels,out_channels", [(6400, 256, 256), (800, 512, 512), (300, 64, 96)])
-def test_pointwise_row_sums(cuda_device, tokens, channels, out_channels):
-    """``row_sums_out``: per token row, the FP64 sum and sum of squares of the
-    stored f16 outputs over all output channels (every column tile adds its
-    part), with a residual in the epilogue as in the transformer's to_out."""
-    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, pack_dense_weight
-
-    g = torch.Generator().manual_seed(tokens + channels)
-    x = torch.randn((2, 1, 1, tokens, channels), generator=g).to(cuda_device, torch.float16)
-    w = (torch.randn((out_channels, channels), generator=g) * channels ** -0.5).to(cuda_device, torch.float16)
-    bias = (torch.randn(out_channels, generator=g) * 0.1).to(cuda_device)
-    res = (torch.randn((2, 1, 1, tokens, out_channels), generator=g) + 2.0).to(cuda_device, torch.float16)
-    sums = torch.zeros((2 * tokens, 2), dtype=torch.float64, device=cuda_device)
-    out = conv3d_ndhwc(x, pack_dense_weight(w), bias, residual=res, row_sums_out=sums)
-    torch.cuda.synchronize()
-    y = out.double().reshape(2 * tokens, out_channels)
-    want = torch.stack([y.sum(1), (y * y).sum(1)], 1)
-    torch.testing.assert_close(sums, want, rtol=1e-6, atol=1e-3)
-    ref = (x.double().reshape(-1, channels) @ w.double().T + bias.double() + res.double().reshape(-1, out_channels))
-    assert ((y - ref).norm() / ref.norm()) < 1e-3
-
-
-@pytest.mark.parametrize("tokens,channels,out_channels,act", [(6400, 256, 768, 0), (800, 512, 2048, 1),
-                                                              (300, 64, 96, 0)])
-def test_folded_layer_norm_dense(cuda_device, tokens, channels, out_channels, act):
-    """``row_sums_in`` + ``fold_layer_norm``: the dense layer of LayerNorm(x)
-    without a LayerNorm pass, against a plain PyTorch fp32 LayerNorm rounded to
-    f16 then the f16 dense layer (and GELU) in fp32 (relative L2 <= 1e-2; the
-    rows carry a large mean so the folded form's cancellation is exercised)."""
-    from lesiondiffusion_mlx_b200 import _lib
-    from lesiondiffusion_mlx_b200.conv import conv3d_ndhwc, fold_layer_norm
-
-    g = torch.Generator().manual_seed(tokens * 7 + out_channels)
-    x = (torch.randn((1, 1, 1, tokens, channels), generator=g) * 1.5 + 4.0).to(cuda_device, torch.float16)
-    w = (torch.randn((out_channels, channels), generator=g) * channels ** -0.5).to(cuda_device, torch.float16)
-    b = (torch.randn(out_channels, generator=g) * 0.1).to(cuda_device, torch.float16).float()
-    gamma = (1.0 + 0.2 * torch.randn(channels, generator=g)).to(cuda_device)
-    beta = (0.2 * torch.randn(channels, generator=g)).to(cuda_device)
-    xr = x.double().reshape(tokens, channels)
-    sums = torch.stack([xr.sum(1), (xr * xr).sum(1)], 1).contiguous()
-    packed, bias, colsum = fold_layer_norm(w, b, gamma, beta)
-    act_code = _lib.LDB_ACT_GELU if act else _lib.LDB_ACT_NONE
-    out = conv3d_ndhwc(x, packed, bias, act=act_code, row_sums_in=sums, col_sums=colsum, row_eps=1e-5)
-    torch.cuda.synchronize()
-    normed = F.layer_norm(x.float().reshape(tokens, channels), (channels,), gamma, beta, 1e-5).half()
-    ref = normed.float() @ w.float().T + b
-    if act:
-        ref = F.gelu(ref.half().float())
-    got = out.float().reshape(tokens, out_channels)
-    err = float((got - ref).norm() / ref.norm())
-    assert err < 1e-2, err
-    assert err < 5e-3, err  # the f16 rounding of W' is the only difference in kind

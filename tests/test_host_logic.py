@@ -187,58 +187,3 @@ def test_one_step_ddim_table_has_positive_strides():
         table = DdimSampler(alphas, steps).coefficients
         assert table.shape == (steps, 5) and all(s > 0 for s in table.strides)
         assert torch.from_numpy(table).shape == (steps, 5)
-
-
-def test_row_norm_entry_point_rejects_what_it_cannot_run():
-    """``ldb_conv3d_fwd_rows`` checks its ``ldb_row_norm`` (layout, required
-    fields) and that the conv is an f16 pointwise one before any device work."""
-    from lesiondiffusion_mlx_b200 import _lib
-
-    desc = _lib.ConvDesc(batch=1, depth=1, height=1, width=64, in_channels=64, x_ld=64, out_channels=64, out_ld=64,
-                         res_ld=64, mode=_lib.LDB_CONV_1X1, exact=0, out_dtype=0, act=0, output_scale=1.0)
-    sums = (ctypes.c_double * 128)()
-    ptr = ctypes.cast(sums, ctypes.c_void_p).value
-
-    def call(rows, d=desc):
-        return _lib.call("ldb_conv3d_fwd_rows", None, ctypes.byref(d), None, None, None, None, None, None,
-                         ctypes.byref(rows), None, 0)
-
-    rows = _lib.RowNorm(sums_out=None, sums_in=None, col_sums=None, eps=1e-5)
-    with pytest.raises(_lib.LdbError, match="neither sums_out nor sums_in"):
-        call(rows)
-    rows.sums_in = ptr
-    with pytest.raises(_lib.LdbError, match="col_sums"):
-        call(rows)
-    rows.struct_size = 16
-    with pytest.raises(_lib.LdbError, match="row_norm struct_size 16"):
-        call(rows)
-    rows = _lib.RowNorm(sums_out=ptr, sums_in=None, col_sums=None, eps=1e-5)
-    desc.mode = _lib.LDB_CONV_3X3X3
-    with pytest.raises(_lib.LdbError, match="f16 pointwise"):
-        call(rows)
-
-
-def test_folded_layer_norm_matches_layer_norm_then_dense():
-    """``fold_layer_norm``: rstd * (x . W' - mean * colsum(W')) + b' is the
-    reference's LayerNorm(x) . W + b (mlx_model.py:360-367, :204-220), up to
-    the f16 rounding of W' (checked in float64 on the CPU)."""
-    from lesiondiffusion_mlx_b200.conv import fold_layer_norm
-
-    rng = np.random.default_rng(11)
-    c, o, n = 192, 80, 64
-    w16 = torch.from_numpy(rng.normal(0, c ** -0.5, (o, c))).to(torch.float16)
-    b16 = torch.from_numpy(rng.normal(0, 0.1, o)).to(torch.float16)
-    gamma = torch.from_numpy(rng.normal(1.0, 0.2, c).astype(np.float32))
-    beta = torch.from_numpy(rng.normal(0.0, 0.2, c).astype(np.float32))
-    x = torch.from_numpy(rng.normal(3.0, 2.0, (n, c))).to(torch.float16).double()  # rows with a large mean
-
-    packed, bias, colsum = fold_layer_norm(w16, b16.float(), gamma, beta)
-    folded = packed.tensor[:o, :c].double()
-    assert packed.tensor.dtype == torch.float16 and not packed.exact
-    assert torch.equal(colsum, folded.sum(1).float())
-    mean = x.mean(1, keepdim=True)
-    rstd = 1.0 / torch.sqrt(x.var(1, unbiased=False, keepdim=True) + 1e-5)
-    got = rstd * (x @ folded.T - mean * colsum.double()) + bias.double()
-    ref = ((x - mean) * rstd * gamma.double() + beta.double()) @ w16.double().T + b16.double()
-    err = (got - ref).norm() / ref.norm()
-    assert err < 2e-3, float(err)
