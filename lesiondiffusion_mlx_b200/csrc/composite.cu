@@ -249,6 +249,9 @@ int ldb_apply_lesion_change(cudaStream_t stream, const float* original, const fl
     return fail(LDB_ERR_INVALID, "apply_lesion_change: null pointer");
   if (n0 <= 0 || n1 <= 0 || n2 <= 0) return fail(LDB_ERR_SHAPE, "apply_lesion_change: extents must be positive");
   if (reach < 0) return fail(LDB_ERR_INVALID, "apply_lesion_change: reach must be >= 0");
+  // A reach of the longest axis already covers every line: larger ones dilate
+  // the same and would only overflow the sweeps' sentinel arithmetic.
+  reach = std::min(reach, std::max(n0, std::max(n1, n2)));
   const long long total = static_cast<long long>(n0) * n1 * n2;
   if (!workspace || workspace_bytes < static_cast<size_t>(2 * total))
     return fail(LDB_ERR_WORKSPACE, "apply_lesion_change needs %lld workspace bytes", 2 * total);

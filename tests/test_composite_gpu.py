@@ -111,3 +111,24 @@ def test_lesion_change_rejects_empty_lesion(cuda_device):
     z = np.zeros((6, 6, 6), np.float32)
     with pytest.raises(ModelExecutionError):
         apply_lesion_change(original=z, generated=z, reconstruction=z, lesion=np.zeros((6, 6, 6), bool))
+
+
+def test_lesion_change_reach_beyond_the_volume(cuda_device):
+    """A reach longer than every axis (here 2^30 voxels) changes exactly what a
+    reach of the longest axis changes: the whole volume."""
+    from lesiondiffusion_mlx_b200.composite import apply_lesion_change
+
+    shape = (12, 20, 9)
+    rng = np.random.default_rng(7)
+    original = _ct(shape, 17)
+    reconstruction = original + rng.normal(size=shape).astype(np.float32)
+    generated = reconstruction + 3.0
+    lesion = np.zeros(shape, bool)
+    lesion[3, 15, 2] = True
+    far, far_facts = apply_lesion_change(original=original, generated=generated, reconstruction=reconstruction,
+                                         lesion=lesion, reach_voxels=2 ** 30)
+    axis, axis_facts = apply_lesion_change(original=original, generated=generated, reconstruction=reconstruction,
+                                           lesion=lesion, reach_voxels=max(shape))
+    assert np.array_equal(far.cpu().numpy(), axis.cpu().numpy())
+    assert far_facts["changed_region"]["voxel_count"] == axis_facts["changed_region"]["voxel_count"] == int(
+        np.prod(shape))
