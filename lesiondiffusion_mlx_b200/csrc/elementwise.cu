@@ -408,6 +408,8 @@ int ldb_timestep_embedding(cudaStream_t stream, const int* timesteps, const int*
   if (!timesteps || !out) return fail(LDB_ERR_INVALID, "timestep_embedding: null pointer");
   if (batch <= 0 || channels <= 0 || channels % 2) return fail(LDB_ERR_SHAPE, "channels must be even and positive");
   if (step && steps <= 0) return fail(LDB_ERR_SHAPE, "timestep_embedding: the step table needs >= 1 row");
+  if (out_dtype != LDB_F16 && out_dtype != LDB_F32)
+    return fail(LDB_ERR_INVALID, "timestep_embedding: out dtype f16 or f32");
   unsigned int* status = device_status_ptr();
   if (!status) return fail(LDB_ERR_CUDA, "timestep_embedding: no device status word");
   const int n = batch * (channels / 2);
@@ -423,6 +425,9 @@ int ldb_dense_small(cudaStream_t stream, const void* x, int x_ld, const void* w,
   if (rows <= 0 || rows > kDenseMaxRows) return fail(LDB_ERR_SHAPE, "dense_small handles 1..%d rows", kDenseMaxRows);
   if (k <= 0 || k % 8 || x_ld % 8) return fail(LDB_ERR_ALIGNMENT, "K and x_ld must be multiples of 8");
   if (n_out <= 0) return fail(LDB_ERR_SHAPE, "n_out must be positive");
+  if (rows > 1 && (x_ld < k || out_ld < n_out))
+    return fail(LDB_ERR_SHAPE, "dense_small: row strides (%d, %d) must cover K %d and n_out %d", x_ld, out_ld, k, n_out);
+  if (out_dtype != LDB_F16 && out_dtype != LDB_F32) return fail(LDB_ERR_INVALID, "dense_small: out dtype f16 or f32");
   const int threads = 256;
   const int blocks = (n_out * 32 + threads - 1) / threads;
   return launch_kernel(dense_small_kernel, dim3(blocks), dim3(threads), 0, stream, "dense_small launch",
@@ -509,6 +514,9 @@ int ldb_resize_nearest(cudaStream_t stream, const void* x, int batch, int in_d, 
   if (!x || !out) return fail(LDB_ERR_INVALID, "resize_nearest: null pointer");
   if (row_bytes <= 0 || row_bytes % 8 || x_row_stride % 8 || out_row_stride % 8)
     return fail(LDB_ERR_ALIGNMENT, "row bytes and strides must be multiples of 8 bytes");
+  if (x_row_stride < row_bytes || out_row_stride < row_bytes)
+    return fail(LDB_ERR_SHAPE, "resize_nearest: row strides (%d, %d) must cover the %d-byte rows", x_row_stride,
+                out_row_stride, row_bytes);
   if (batch <= 0 || in_d <= 0 || in_h <= 0 || in_w <= 0 || out_d <= 0 || out_h <= 0 || out_w <= 0)
     return fail(LDB_ERR_SHAPE, "resize_nearest: extents must be positive");
   const long long total = static_cast<long long>(batch) * out_d * out_h * out_w * (row_bytes / 8);
@@ -524,6 +532,8 @@ int ldb_resize_nearest(cudaStream_t stream, const void* x, int batch, int in_d, 
 int ldb_hu_map(cudaStream_t stream, const void* x, int dtype, int x_ld, long long n, float* out) {
   using namespace ldb;
   if (!x || !out || n <= 0) return fail(LDB_ERR_INVALID, "hu_map: bad arguments");
+  if (dtype != LDB_F16 && dtype != LDB_F32) return fail(LDB_ERR_INVALID, "hu_map: input dtype f16 or f32");
+  if (x_ld < 1) return fail(LDB_ERR_SHAPE, "hu_map: x_ld must be positive");
   const int threads = 256;
   return launch_kernel(hu_map_kernel, dim3(static_cast<unsigned>((n + threads - 1) / threads)), dim3(threads), 0,
                        stream, "hu_map launch", x, int(dtype == LDB_F32), x_ld, n, out);

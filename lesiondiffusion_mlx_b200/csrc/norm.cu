@@ -728,6 +728,7 @@ int ldb_layer_norm_ex(cudaStream_t stream, const void* x, int x_dtype, int x_ld,
   if (channels <= 0 || channels > 1024 || channels % 8) return fail(LDB_ERR_SHAPE, "channels must be 8..1024, %% 8");
   const int cpad = split ? (channels + 15) / 16 * 16 : channels;
   if (x_ld % 8 || out_ld % 8) return fail(LDB_ERR_ALIGNMENT, "row strides must be multiples of 8");
+  if (x_ld < channels) return fail(LDB_ERR_SHAPE, "layer_norm: x_ld %d < %d channels", x_ld, channels);
   if (out_ld < (split ? 2 * cpad : channels)) return fail(LDB_ERR_SHAPE, "out_ld too small");
   if (rows <= 0) return fail(LDB_ERR_SHAPE, "rows must be positive");
   const int threads = 256;

@@ -187,3 +187,25 @@ def test_one_step_ddim_table_has_positive_strides():
         table = DdimSampler(alphas, steps).coefficients
         assert table.shape == (steps, 5) and all(s > 0 for s in table.strides)
         assert torch.from_numpy(table).shape == (steps, 5)
+
+
+def test_entry_points_reject_rows_their_strides_do_not_cover():
+    """Row strides shorter than the rows they step over, and element types a
+    kernel does not read, fail with an error before any launch (checked
+    without a device: the pointers are host placeholders never dereferenced)."""
+    from lesiondiffusion_mlx_b200 import _lib
+
+    buf = (ctypes.c_char * 64)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    cases = [
+        ("ldb_layer_norm_ex", (None, p, _lib.LDB_F16, 32, p, p, 1e-5, p, 64, 4, 64, 0), "x_ld 32 < 64"),
+        ("ldb_dense_small", (None, p, 8, p, None, p, 64, 2, 64, 16, 0, 0, _lib.LDB_F16, 0), "must cover K 16"),
+        ("ldb_dense_small", (None, p, 16, p, None, p, 64, 2, 64, 16, 0, 0, _lib.LDB_BF16, 0), "out dtype"),
+        ("ldb_hu_map", (None, p, _lib.LDB_F16, 0, 10, p), "x_ld must be positive"),
+        ("ldb_hu_map", (None, p, _lib.LDB_BF16, 1, 10, p), "input dtype"),
+        ("ldb_resize_nearest", (None, p, 1, 2, 2, 2, 16, 8, p, 4, 4, 4, 16), "cover the 16-byte rows"),
+        ("ldb_timestep_embedding", (None, p, None, 1, 2, 32, p, _lib.LDB_BF16), "out dtype"),
+    ]
+    for name, args, message in cases:
+        with pytest.raises(_lib.LdbError, match=message):
+            _lib.call(name, *args)
