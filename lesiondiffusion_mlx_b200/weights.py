@@ -43,8 +43,18 @@ def read_safetensors(path: str | Path) -> dict[str, np.ndarray]:
     for name, info in header.items():
         if name == "__metadata__":
             continue
-        begin, end = info["data_offsets"]
+        begin, end = (int(v) for v in info["data_offsets"])
         shape = tuple(int(s) for s in info["shape"])
+        if not 0 <= begin <= end <= len(body):
+            raise ValueError(f"{path}: {name} data offsets [{begin}, {end}) lie outside the {len(body)}-byte body")
+        if any(s < 0 for s in shape):
+            raise ValueError(f"{path}: {name} has a negative extent in shape {shape}")
+        itemsize = 2 if info["dtype"] == "BF16" else (np.dtype(_NP[info["dtype"]]).itemsize if info["dtype"] in _NP
+                                                        else 0)
+        count = int(np.prod(shape)) if shape else 1
+        if itemsize and end - begin != count * itemsize:
+            raise ValueError(f"{path}: {name} holds {end - begin} bytes, shape {shape} of {info['dtype']} needs "
+                             f"{count * itemsize}")
         raw = body[begin:end]
         if info["dtype"] == "BF16":
             bits = np.frombuffer(raw, dtype="<u2").astype(np.uint32) << 16
@@ -53,9 +63,6 @@ def read_safetensors(path: str | Path) -> dict[str, np.ndarray]:
             arr = np.frombuffer(raw, dtype=np.dtype(_NP[info["dtype"]]).newbyteorder("<"))
         else:
             raise ValueError(f"{path}: unsupported dtype {info['dtype']} for {name}")
-        count = int(np.prod(shape)) if shape else 1
-        if arr.size != count:
-            raise ValueError(f"{path}: {name} holds {arr.size} elements, shape {shape} needs {count}")
         out[name] = arr.reshape(shape).copy()
     return out
 

@@ -69,3 +69,21 @@ def test_truncated_file_is_rejected(tmp_path):
     (tmp_path / "bad.safetensors").write_bytes(data[:-10])
     with pytest.raises(ValueError):
         read_safetensors(tmp_path / "bad.safetensors")
+
+
+@pytest.mark.parametrize("offsets,shape,message", [
+    ([-8, 8], [2], "outside"),          # a negative start would slice from the end of the body
+    ([8, 4], [1], "outside"),           # end before begin
+    ([0, 24], [2], "outside"),          # past the 16-byte body
+    ([0, 12], [2], "holds 12 bytes"),   # not the shape's byte count
+    ([0, 8], [-2], "negative extent"),
+])
+def test_tensor_records_outside_or_inconsistent_with_the_body_are_rejected(tmp_path, offsets, shape, message):
+    """Each tensor's data offsets must lie inside the body and span exactly its
+    shape's bytes; anything else is a ValueError, never a silent misread."""
+    header = json.dumps({"x": {"dtype": "F32", "shape": shape, "data_offsets": offsets}}).encode()
+    header += b" " * (-len(header) % 8)
+    path = tmp_path / "bad.safetensors"
+    path.write_bytes(struct.pack("<Q", len(header)) + header + np.arange(4, dtype="<f4").tobytes())
+    with pytest.raises(ValueError, match=message):
+        read_safetensors(path)
