@@ -20,7 +20,7 @@ from .conv import pack_weight as _pack
 
 __all__ = [
     "nax_available", "nax_eligible", "pack_weight", "pack_upsample_weight", "nax_conv3d", "flash_eligible",
-    "flash_attention", "group_norm_affine", "native_group_norm", "nearest_codebook4", "upsample_nearest2",
+    "flash_attention", "flash_attention_half", "group_norm_affine", "native_group_norm", "nearest_codebook4", "upsample_nearest2",
     "resize_nearest", "piecewise_ct",
 ]
 
@@ -135,6 +135,18 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
                     mx=None) -> torch.Tensor:
     """Multi-head attention on head-interleaved projections (_attention.py:331-375)."""
     return ops.flash_attention(q.contiguous(), k.contiguous(), v.contiguous(), heads=heads, scale=scale)
+
+
+def flash_attention_half(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, scale: float,
+                         mx=None) -> torch.Tensor:
+    """FP16 attention on head-interleaved projections, returning q's shape in
+    float16 (_attention_half.py:129-147).  The reference's kernel takes 32-wide
+    heads over equal query / key lengths that are multiples of 32 and leaves that
+    dispatch to the caller; the tcgen05 kernel here also takes 16- and 64-wide
+    heads and any lengths, with the same result where both apply."""
+    if not (q.dtype == k.dtype == v.dtype == torch.float16):
+        raise ValueError(f"flash_attention_half takes float16 projections, got {q.dtype}, {k.dtype}, {v.dtype}")
+    return flash_attention(q, k, v, heads=heads, scale=scale)
 
 
 def group_norm_affine(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, *, groups: int, eps: float,

@@ -89,6 +89,8 @@ def test_attention_eligibility():
     assert not api.flash_eligible(q, q.float(), 4)
     assert not api.flash_eligible(q.float(), q.float(), 4)
     assert not api.flash_eligible(q, torch.zeros((1, 10, 128), dtype=torch.float16), 4)
+    with pytest.raises(ValueError, match="float16 projections"):
+        api.flash_attention_half(q.to(torch.bfloat16), q.to(torch.bfloat16), q.to(torch.bfloat16), heads=8, scale=0.2)
 
 
 def test_other_operator_argument_errors():

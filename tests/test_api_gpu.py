@@ -152,6 +152,24 @@ def test_flash_attention(cuda_device, dtype, lq, lk):
     assert rel_l2(out.float().cpu().numpy(), want.float().numpy()) <= 1e-2
 
 
+@pytest.mark.parametrize("length", [256, 300])
+def test_flash_attention_half(cuda_device, length):
+    """The FP16 entry point on the reference kernel's case (32-wide heads, equal
+    query and key lengths; 300 is not a multiple of 32, which the reference
+    leaves to its caller) against the oracle's restatement of the reference's
+    FP16 flash contract."""
+    from lesiondiffusion_mlx_b200 import api
+
+    rng = np.random.default_rng(length)
+    q, k, v = (torch.from_numpy(rng.normal(size=(2, length, 8 * 32)).astype(np.float32)).half() for _ in range(3))
+    out = api.flash_attention_half(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), heads=8,
+                                   scale=32 ** -0.5, mx=None)
+    torch.cuda.synchronize()
+    want = oops.attention(q, k, v, heads=8, scale=32 ** -0.5)
+    assert out.dtype == torch.float16 and tuple(out.shape) == tuple(q.shape)
+    assert rel_l2(out.float().cpu().numpy(), want.float().numpy()) <= 1e-2
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_nearest_codebook4(cuda_device, dtype):
     """int32 indices, bit-exact with the oracle's rounding order, ties to the first index."""
