@@ -20,7 +20,8 @@ from .conv import pack_weight as _pack
 
 __all__ = [
     "nax_available", "nax_eligible", "pack_weight", "pack_upsample_weight", "nax_conv3d", "flash_eligible",
-    "flash_attention", "flash_attention_half", "group_norm_affine", "native_group_norm", "nearest_codebook4", "upsample_nearest2",
+    "flash_attention", "flash_attention_half", "group_norm_affine", "native_group_norm",
+    "native_group_norm_eligible", "nearest_codebook4", "upsample_nearest2",
     "resize_nearest", "piecewise_ct",
 ]
 
@@ -154,6 +155,18 @@ def group_norm_affine(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
     """Flat ``(B * C * 2)`` FP32 ``(scale, offset)`` pairs of GroupNorm on NCDHW ``x``."""
     affine = ops.group_norm_affine(_to_ndhwc(x), weight, bias, groups=groups, eps=eps)
     return affine.reshape(-1)
+
+
+def native_group_norm_eligible(x: torch.Tensor, groups: int, mx=None) -> bool:
+    """Whether ``group_norm_affine`` / ``native_group_norm`` take ``x`` with ``groups``
+    groups: the predicate the reference's layers test before their native
+    GroupNorm (medmlx-core, called at mlx_model.py:240, :268, :321).  Here: a
+    5-D NCDHW float16 / float32 tensor whose channels are a multiple of 8 that
+    ``groups`` divides, at most 1024 channels per group and 8192 in all."""
+    if x.ndim != 5 or x.dtype not in (torch.float16, torch.float32) or groups <= 0:
+        return False
+    c = int(x.shape[1])
+    return c % 8 == 0 and c % groups == 0 and c // groups <= 1024 and c <= 8192
 
 
 def native_group_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, *, groups: int, eps: float,

@@ -100,3 +100,16 @@ def test_other_operator_argument_errors():
         api.resize_nearest(torch.zeros((1, 1, 2, 2, 2)), (4, 4))
     with pytest.raises(ValueError, match="CUDA"):
         api.piecewise_ct(torch.zeros(3), inverse=False)  # device kernels take device tensors only
+
+
+def test_native_group_norm_eligibility():
+    """The predicate the reference tests before its native GroupNorm, answered
+    with the limits of the GroupNorm kernels here."""
+    x = torch.zeros((1, 64, 2, 2, 2), dtype=torch.float16)
+    assert api.native_group_norm_eligible(x, 32)
+    assert api.native_group_norm_eligible(x.float(), 16)
+    assert not api.native_group_norm_eligible(x.to(torch.bfloat16), 32)  # f16 / f32 only
+    assert not api.native_group_norm_eligible(x, 24)  # groups must divide the channels
+    assert not api.native_group_norm_eligible(torch.zeros((1, 12, 2, 2, 2), dtype=torch.float16), 12)  # 12 % 8
+    assert not api.native_group_norm_eligible(torch.zeros((1, 2048, 1, 1, 1), dtype=torch.float16), 1)  # > 1024 per group
+    assert not api.native_group_norm_eligible(torch.zeros((1, 64, 4), dtype=torch.float16), 32)  # not NCDHW
