@@ -508,6 +508,28 @@ class LdmUnetB200(_Layers):
     def __call__(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor | None) -> torch.Tensor:
         return self.forward(x, timesteps, self.prepare_context(context))
 
+    def prepare_denoiser(self, context: torch.Tensor | None) -> "BoundDenoiser":
+        """Bind ``context`` and project its cross-attention keys / values once
+        (mlx_model.py:570-597): the result is ``denoise(x, timesteps)``, and the
+        samplers' ``prepare`` takes it.  Its projections belong to this binding."""
+        return BoundDenoiser(self, self.prepare_context(context))
+
+
+class BoundDenoiser:
+    """A UNet bound to one context (``LdmUnetB200.prepare_denoiser``).
+
+    ``denoise(x, timesteps)`` predicts the noise of the network input ``x``
+    (NDHWC, the layout of ``LdmUnetB200.forward``; the reference's callable
+    takes NCDHW MLX arrays) with the binding's precomputed cross-attention
+    keys and values."""
+
+    def __init__(self, unet: LdmUnetB200, cache: dict):
+        self.unet = unet
+        self.cache = cache
+
+    def __call__(self, x: torch.Tensor, timesteps: torch.Tensor) -> torch.Tensor:
+        return self.unet.forward(x, timesteps, self.cache)
+
 
 class VqDecoderB200(_Layers):
     """VQ quantize + decode (mlx_model.py:742-819) on B200 kernels, NDHWC.

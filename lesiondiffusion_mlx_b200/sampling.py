@@ -83,6 +83,11 @@ class DdimSampler:
     def steps(self) -> int:
         return len(self.timesteps)
 
+    def prepare(self, denoiser, conditioning_image: torch.Tensor, *, mask: torch.Tensor | None = None,
+                generator: torch.Generator | None = None):
+        """``sample()`` for a context-bound denoiser (``prepare_sample``)."""
+        return prepare_sample(self, denoiser, conditioning_image, mask=mask, generator=generator)
+
 
 class Dpmpp2mSampler:
     """Deterministic DPM-Solver++ 2M, Diffusers-0.42.1 midpoint (_dpm.py:21-153).
@@ -119,6 +124,50 @@ class Dpmpp2mSampler:
     @property
     def steps(self) -> int:
         return len(self.timesteps)
+
+    def prepare(self, denoiser, conditioning_image: torch.Tensor, *, mask: torch.Tensor | None = None,
+                generator: torch.Generator | None = None):
+        """``sample()`` for a context-bound denoiser (``prepare_sample``)."""
+        return prepare_sample(self, denoiser, conditioning_image, mask=mask, generator=generator)
+
+
+def prepare_sample(sampler, denoiser, conditioning_image: torch.Tensor, *, mask: torch.Tensor | None = None,
+                   generator: torch.Generator | None = None, graph: bool = True):
+    """The reference's ``Sampler.prepare(denoiser, conditioning_image, mask=)``
+    (mlx_sampling.py:138-200, _dpm.py:82-100) on the B200 step.
+
+    ``denoiser`` is what ``LdmUnetB200.prepare_denoiser`` returns;
+    ``conditioning_image`` is NCDHW (the known latent with a mask, the
+    concatenated image without one) and ``mask`` ``(B, 1, D, H, W)``, as in the
+    reference.  The returned ``sample()`` draws a fresh initial noise (and, for
+    DDIM, one noise tensor per step) from ``generator`` on the device, runs the
+    whole trajectory (one captured CUDA graph per step with ``graph``) and
+    returns the NCDHW float32 sample, the known region re-imposed.  The draws
+    come from torch's generator, not MLX's, so the noise itself differs from
+    the reference's."""
+    if not (hasattr(denoiser, "unet") and hasattr(denoiser, "cache")):
+        raise TypeError("prepare takes the denoiser that LdmUnetB200.prepare_denoiser returns")
+    if conditioning_image.ndim != 5:
+        raise ValueError(f"conditioning_image must be NCDHW, got shape {tuple(conditioning_image.shape)}")
+    dev = denoiser.unet.device
+    image = conditioning_image.to(dev, torch.float32).permute(0, 2, 3, 4, 1).contiguous()
+    m = None
+    if mask is not None:
+        b, _, d, h, w = conditioning_image.shape
+        if tuple(mask.shape) != (b, 1, d, h, w):
+            raise ValueError(f"mask must be {(b, 1, d, h, w)}, got {tuple(mask.shape)}")
+        m = mask.to(dev, torch.float32)[:, 0].contiguous()
+    prepared = PreparedSampler(sampler, denoiser.unet, denoiser.cache, image, m, graph=graph)
+
+    def sample() -> torch.Tensor:
+        s = prepared.state
+        initial = torch.randn(tuple(s.x.shape), generator=generator, device=dev)
+        step_noise = torch.randn(tuple(s.noise.shape), generator=generator, device=dev) \
+            if sampler.kind == KIND_DDIM else None
+        return prepared.run(initial, step_noise).permute(0, 4, 1, 2, 3).clone()
+
+    sample.prepared = prepared
+    return sample
 
 
 @dataclass

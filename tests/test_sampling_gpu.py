@@ -103,3 +103,4 @@ def test_step_counter_past_the_tables_touches_nothing(cuda_device):
     assert torch.equal(x, moved) and torch.equal(emb, emb_before)
     assert _lib.device_status(reset=True) & 2
     assert _lib.device_status(reset=False) == 0
+
