@@ -209,3 +209,36 @@ def test_entry_points_reject_rows_their_strides_do_not_cover():
     for name, args, message in cases:
         with pytest.raises(_lib.LdbError, match=message):
             _lib.call(name, *args)
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes signature of the binding has the parameters of its
+    declaration in ``include/ldb200.h``, in order and by kind (pointer, int,
+    float, double, 64-bit integer), and the declared return type: a binding
+    that drifts from the header (a parameter added on one side only) fails here
+    instead of shifting every later argument at run time."""
+    from lesiondiffusion_mlx_b200 import _lib
+
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "ldb200.h").read_text(), flags=re.S)
+
+    def c_kind(param: str) -> str:
+        param = re.sub(r"\bconst\b", "", param).strip()
+        if "*" in param or param.startswith("ldb_stream_t"):
+            return "ptr"
+        base = re.sub(r"\s+\w+$", "", param).strip()  # drop the parameter name
+        return {"long long": "i64", "unsigned int": "uint", "unsigned long long": "u64", "size_t": "u64"}.get(base, base)
+
+    def py_kind(t) -> str:
+        if t is ctypes.c_void_p or t is ctypes.c_char_p or (isinstance(t, type) and issubclass(t, ctypes._Pointer)):
+            return "ptr"
+        # (ctypes makes c_size_t the same type as c_ulonglong on 64-bit Linux: both are "u64")
+        return {ctypes.c_int: "int", ctypes.c_float: "float", ctypes.c_double: "double", ctypes.c_size_t: "u64",
+                ctypes.c_longlong: "i64", ctypes.c_uint: "uint", ctypes.c_ulonglong: "u64"}[t]
+
+    declared = re.findall(r"LDB_API\s+([^;(]*?)\b(ldb_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.S)
+    assert len(declared) == len(declared_symbols())
+    for ret, name, params in declared:
+        params = params.strip()
+        kinds = [] if params in ("", "void") else [c_kind(p) for p in params.split(",")]
+        assert [py_kind(t) for t in _lib.SIGNATURES[name]] == kinds, name
+        assert py_kind(_lib._RESTYPES.get(name, ctypes.c_int)) == c_kind(ret.strip() + " r"), name
