@@ -242,3 +242,20 @@ def test_ctypes_signatures_match_the_header():
         kinds = [] if params in ("", "void") else [c_kind(p) for p in params.split(",")]
         assert [py_kind(t) for t in _lib.SIGNATURES[name]] == kinds, name
         assert py_kind(_lib._RESTYPES.get(name, ctypes.c_int)) == c_kind(ret.strip() + " r"), name
+
+
+def test_conv_descriptor_fields_match_the_header():
+    """``_lib.ConvDesc`` lists the fields of ``ldb_conv_desc`` in the header's
+    order with the same kinds (the size check alone would pass two swapped
+    fields of one type)."""
+    from lesiondiffusion_mlx_b200 import _lib
+
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "ldb200.h").read_text(), flags=re.S)
+    body = re.search(r"typedef struct \{(.*?)\}\s*ldb_conv_desc;", text, flags=re.S).group(1)
+    fields = []
+    for decl in filter(None, (d.strip() for d in body.split(";"))):
+        kind = "ptr" if "*" in decl else decl.split()[0]
+        names = decl.replace("*", " ").split(None, 1)[1] if kind != "ptr" else decl.split("*")[-1]
+        fields += [(n.strip(), kind) for n in names.split(",")]
+    kinds = {ctypes.c_int: "int", ctypes.c_float: "float", ctypes.c_void_p: "ptr"}
+    assert [(n, kinds[t]) for n, t in _lib.ConvDesc._fields_] == fields
