@@ -621,7 +621,7 @@ int ldb_group_norm_affine(cudaStream_t stream, const void* x1, int c1, int ld1, 
                           int dtype, int batch, int voxels, int groups, const float* gamma, const float* beta,
                           float eps, float* affine, void* workspace, size_t workspace_bytes) {
   using namespace ldb;
-  Src2 s;
+  Src2 s{};
   int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
   if (rc != LDB_OK) return rc;
   const int C = s.c1 + s.c2;
@@ -661,7 +661,7 @@ int ldb_prepare_input(cudaStream_t stream, const void* x1, int c1, int ld1, cons
                       int dtype, int batch, int voxels, const float* affine, int silu, int split, void* out,
                       int out_ld) {
   using namespace ldb;
-  Src2 s;
+  Src2 s{};
   int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
   if (rc != LDB_OK) return rc;
   if (!out) return fail(LDB_ERR_INVALID, "out is null");
@@ -698,7 +698,7 @@ int ldb_prepare_input_from_stats(cudaStream_t stream, const void* x1, int c1, in
                                  const double* stats2, int groups, const float* gamma, const float* beta, float eps,
                                  int silu, int split, void* out, int out_ld) {
   using namespace ldb;
-  Src2 s;
+  Src2 s{};
   int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
   if (rc != LDB_OK) return rc;
   if (!out || !stats1 || (s.c2 > 0 && !stats2)) return fail(LDB_ERR_INVALID, "prepare from stats: null pointer");
@@ -760,7 +760,7 @@ int ldb_group_norm_affine_noalloc(cudaStream_t stream, const void* x1, int c1, i
                                   int ld2, int dtype, int batch, int voxels, int groups, const float* gamma,
                                   const float* beta, float eps, float* affine) {
   using namespace ldb;
-  Src2 s;
+  Src2 s{};
   int rc = make_src(x1, c1, ld1, x2, c2, ld2, dtype, &s);
   if (rc != LDB_OK) return rc;
   const int C = s.c1 + s.c2;
